@@ -1,0 +1,177 @@
+/*
+ * swann_b200.h -- C ABI of the B200 (sm_100a) SWANN search and graph build.
+ *
+ * Plain pointers, sizes, knobs and a cudaStream_t (passed as void*); no torch
+ * types.  Every buffer is caller-owned device memory unless a comment says
+ * otherwise; the calls are asynchronous on `stream` and never synchronise.
+ * Each returns SWB_OK or an SWB_ERR_* code; swb_last_error() describes the
+ * last failure on the calling thread.
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * geniussyn/SWANN).  The reference binds its kernels through pybind
+ * (swann/csrc/local_search.cu:950-955) and torch (swann/build.py); a
+ * maintainer binds these through ctypes instead.
+ */
+#ifndef SWANN_B200_H
+#define SWANN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SWB_API __attribute__((visibility("default")))
+#else
+#define SWB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define SWB_OK 0
+#define SWB_ERR_ARG 1       /* a shape, size, pointer or knob is invalid */
+#define SWB_ERR_TEAM 2      /* team size is not 4, 8, 16 or 32 */
+#define SWB_ERR_SMEM 3      /* the configuration needs more shared memory than a block may have */
+#define SWB_ERR_BATCH 4     /* more than 65535 queries in one call */
+#define SWB_ERR_CUDA 5      /* a CUDA runtime call or launch failed */
+#define SWB_ERR_TIMEOUT 6   /* a bounded device-side wait gave up (read from the status word) */
+
+/* element types of the corpus */
+#define SWB_F32 0
+#define SWB_F16 1
+
+/* metrics and policies (swann/_engine.py:31-36) */
+#define SWB_METRIC_IP 0     /* distance = 1 - <q, x>, rows L2-normalised */
+#define SWB_METRIC_L2 1     /* distance = |q - x|^2 */
+#define SWB_POLICY_BEST 0
+#define SWB_POLICY_ROUND_ROBIN 1
+
+#define SWB_NCTR 10         /* per-branch counters, local_search.cu:35-41 */
+
+/* Limits of the kernels (the reference's MAXL, MAXD and lineage width). */
+#define SWB_MAX_QUEUE 512
+#define SWB_MAX_DEGREE 128
+#define SWB_MAX_SEEDS 128
+#define SWB_MAX_BATCH 65535
+
+/* ---------------------------------------------------------------- search -- */
+
+/* Replaces init_states (swann/csrc/local_search.cu:741-776, launched from
+ * swann/_engine.py:219-278).  One state per (query, branch): scores the V seeds
+ * of each branch, writes its queue, clears its visited table and counters, and
+ * clears the per-query distance table and bound when they are given.
+ *   X        [n, dim] SWB_F32 or SWB_F16 rows; dim % 4 == 0 (f32) or % 8 == 0 (f16)
+ *   Qv       [Q, dim] float32 queries
+ *   seeds    [Q, J, V] int32, -1 = empty
+ *   ids/dist/expanded/lineage  [Q, J, L] int32 / float32 / uint8 / uint8 (out)
+ *   visited  [Q, J, H] int32, H a power of two; H == 1 switches it off
+ *   counters [Q, J, SWB_NCTR] int32 (out)
+ *   cache    [Q, Hc] uint64 per-query distance table (key id+1 in the high word,
+ *            float bits of the distance in the low word); NULL / Hc == 0 = off
+ *   bound    [Q] float32 per-query k-th-best bound; NULL = off */
+SWB_API int swb_search_init(const void* X, int x_dtype, int64_t n, int dim,
+                    const float* Qv, const int32_t* seeds, int Q, int J, int V,
+                    int32_t* ids, float* dist, uint8_t* expanded, uint8_t* lineage, int L,
+                    int32_t* visited, int H, int32_t* counters,
+                    int metric, int team,
+                    uint64_t* cache, int Hc, float* bound,
+                    void* stream);
+
+/* Replaces advance (swann/csrc/local_search.cu:778-841, swann/_engine.py:281-317).
+ * Advances every branch (or the `n_active` flattened q*J+j indices in
+ * `active`) by up to `delta` expansions, in place; resumable: advance(a) then
+ * advance(b) equals advance(a + b).
+ *   G        [n, D] int32 adjacency, -1 = no edge, D <= SWB_MAX_DEGREE
+ *   status   optional int32 device word; a device-side wait that runs out sets
+ *            it to SWB_ERR_TIMEOUT (never set in normal operation) */
+SWB_API int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim,
+                       const int32_t* G, int D, const float* Qv,
+                       int32_t* ids, float* dist, uint8_t* expanded, uint8_t* lineage,
+                       int Q, int J, int L,
+                       int32_t* visited, int H, int32_t* counters,
+                       int metric, int team, int delta, int max_expansions,
+                       int policy, int V, float stop_eps, int kstop,
+                       uint64_t* cache, int Hc, float* bound, int exclusive,
+                       int stall_patience, float crowd_frac,
+                       const int32_t* active, int n_active,
+                       int32_t* status, void* stream);
+
+/* Replaces merge_branches (swann/csrc/local_search.cu:925-947, and the tensor
+ * definition swann/_engine.py:377-402): per query, the k nearest of the J*kk
+ * branch results by (distance, id), each id once; padding is (-1, +inf). */
+SWB_API int swb_merge_branches(const int32_t* bids, const float* bdist, int Q, int J, int kk, int k,
+                       int32_t* out_ids, float* out_dist, void* stream);
+
+/* Clears what a fused search shares per query: the distance table, the bound
+ * and the per-query completion counter.  Launch before swb_search_fused on the
+ * same stream.  Part of replacing init_kernel's clears (local_search.cu:302-313). */
+SWB_API int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int32_t* qdone,
+                       void* stream);
+
+/* Replaces the whole of swann/_engine.py:428-447 (search: init_states, advance
+ * for the full budget, branch_topk, merge_branches) as one kernel, the path
+ * swann/index.py:86-110 (Index.search) runs.  The last branch of each query to
+ * finish merges that query's branches.
+ *   branch_ids/branch_dist [Q, J, kk] int32/float32 scratch, kk = min(k, L)
+ *   qdone    [Q] int32, cleared by swb_search_prepare
+ *   out_ids/out_dist [Q, k] (out)
+ *   ids/dist/expanded/lineage/counters: optional outputs of the final branch
+ *   states (NULL to skip), shapes as in swb_search_init */
+SWB_API int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim,
+                     const int32_t* G, int D, const float* Qv, const int32_t* seeds,
+                     int Q, int J, int V, int k, int L, int B,
+                     int metric, int team, int policy, float stop_eps, int kstop,
+                     int32_t* visited, int H,
+                     uint64_t* cache, int Hc, float* bound, int exclusive,
+                     int stall_patience, float crowd_frac,
+                     int32_t* branch_ids, float* branch_dist, int32_t* qdone,
+                     int32_t* out_ids, float* out_dist,
+                     int32_t* ids, float* dist, uint8_t* expanded, uint8_t* lineage,
+                     int32_t* counters, int32_t* status, void* stream);
+
+/* ----------------------------------------------------------------- build -- */
+
+/* Replaces the selection half of knn_candidates (swann/build.py:36-42:
+ * pairwise, the 3.4e38 diagonal, torch.topk): folds a block of dot products
+ * dots[r * ld + c] = <x_{row0+r}, x_{col0+c}> (rows x ncols) into each row's
+ * running C nearest, ascending by (distance, id).  resume = 0 starts the lists;
+ * resume = 1 continues the lists idx/dst already hold (column blocking).
+ *   ip: 1 - <a, b>      l2: max((|b|^2 - 2<a, b>) + |a|^2, 0)
+ *   norms    [n] float32 squared row norms (l2 only; NULL for ip)
+ *   idx/dst  [rows, C] int32 / float32, C <= 256 */
+SWB_API int swb_topc_block(const float* dots, int64_t rows, int64_t ld, int64_t ncols, int64_t row0,
+                   int64_t col0, const float* norms, int metric, int C, int32_t* idx, float* dst,
+                   int resume, void* stream);
+
+/* Squared norms of the rows of X in sequential-fmaf order (the build's l2 norms). */
+SWB_API int swb_row_norms(const void* X, int x_dtype, int64_t n, int dim, float* norms, void* stream);
+
+/* Replaces robust_prune (swann/build.py:48-91): keeps candidate i of node u
+ * unless an already-kept j has alpha * pair(j, i) <= cdist[u, i]; at most `deg`
+ * kept, written in candidate order and padded with -1.
+ *   X [n, dim] f32 rows (fp16 corpora are built in fp32, build.py:165-166)
+ *   cand/cdist [rows, C] int32 / float32, C <= 128;  out [rows, deg] int32 */
+SWB_API int swb_prune(const float* X, int64_t n, int dim, const int32_t* cand, const float* cdist,
+              int64_t rows, int C, int deg, float alpha, int metric, int32_t* out, void* stream);
+
+/* Replaces add_reverse (swann/build.py:96-150): offers every edge of G back to
+ * its target (first `max_in` offers per target in source order), merges with
+ * the target's own row, drops self and duplicates, scores, keeps the nearest
+ * 128 and re-prunes to `deg` -- for rows [row0, row0 + rows) (a rank's row
+ * block; the whole graph is row0 = 0, rows = n).
+ *   G [n, deg] int32;  out [rows, deg] int32 (must not alias G)
+ *   workspace: at least swb_reverse_workspace(n, rows, deg, max_in) bytes */
+SWB_API int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G, int deg, float alpha,
+                int max_in, int metric, int64_t row0, int64_t rows, int32_t* out,
+                void* workspace, uint64_t ws_bytes, void* stream);
+SWB_API uint64_t swb_reverse_workspace(int64_t n, int64_t rows, int deg, int max_in);
+
+/* --------------------------------------------------------------- utility -- */
+
+SWB_API const char* swb_last_error(void);
+SWB_API int swb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SWANN_B200_H */

@@ -1,0 +1,153 @@
+"""Graph construction: exact candidates, a detour-pruning pass, reverse edges.
+
+Drop-in for swann/build.py (geniussyn/SWANN): `pairwise`, `knn_candidates`,
+`robust_prune`, `add_reverse`, `build_graph`, same arguments and results.
+
+  knn_candidates  exact top-C by the metric, self excluded.  A chunk of rows
+                  is scored against the whole corpus and each row's C nearest
+                  are selected by swb_topc_block (native); the dot products of
+                  the chunk come from a tensor-core GEMM.
+  robust_prune    swb_prune: one block per node, the candidates' Gram matrix
+                  in shared memory, the reference's sequential keep rule.
+  add_reverse     swb_reverse: stable radix sort of the edges by target, row
+                  merge + scoring, then the same prune.
+
+The prune and reverse passes accumulate every dot product in dimension order
+with fmaf, so their output is reproducible bit for bit from the same input.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as N
+from ._engine import METRIC_IP, METRIC_L2
+
+_METRIC = {"ip": METRIC_IP, "l2": METRIC_L2}
+
+
+def _m(metric) -> int:
+    if isinstance(metric, str):
+        if metric not in _METRIC:
+            raise ValueError(f"metric must be one of {sorted(_METRIC)}")
+        return _METRIC[metric]
+    return int(metric)
+
+
+def pairwise(A, B, metric, bn=None):
+    """Distances from every row of A to every row of B, in the corpus's metric
+    (swann/build.py:14-25).  Library GEMM; kept for API parity."""
+    if _m(metric) == METRIC_IP:
+        return 1.0 - (A @ B.T)
+    if bn is None:
+        bn = (B * B).sum(1)
+    return (bn.view(1, -1) - 2.0 * (A @ B.T) + (A * A).sum(1).view(-1, 1)).clamp(min=0)
+
+
+def row_norms(Xg):
+    out = torch.empty(Xg.shape[0], dtype=torch.float32, device=Xg.device)
+    with torch.cuda.device(Xg.device):
+        N.check(N.lib().swb_row_norms(N.ptr(Xg), N.dtype_code(Xg), Xg.shape[0], Xg.shape[1], N.ptr(out),
+                                      N.stream_of(Xg)), "row_norms")
+    return out
+
+
+def _dots(A, B, exact_half):
+    """A @ B.T in fp32.  fp16-valued rows multiply exactly in TF32 (11-bit
+    significands), so their products are exact and only the accumulation
+    order differs from a plain fp32 GEMM."""
+    if exact_half:
+        try:
+            return torch.mm(A.half(), B.half().T, out_dtype=torch.float32)
+        except (RuntimeError, TypeError):
+            pass
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = bool(exact_half)
+    try:
+        return A @ B.T
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@torch.no_grad()
+def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact=None):
+    """Exact top-C neighbours by the corpus's metric, self excluded
+    (swann/build.py:30-43).  Returns (idx int32 [n, C], dst f32 [n, C])."""
+    m = _m(metric)
+    if not Xg.is_cuda:
+        raise ValueError("vectors must be on the GPU")
+    Xg = Xg.contiguous()
+    n = Xg.shape[0]
+    if half_exact is None:
+        small = n * Xg.shape[1] <= (1 << 26)
+        half_exact = bool(Xg.dtype == torch.float16 or (small and torch.equal(Xg, Xg.half().float())))
+    Xf = Xg.float().contiguous()
+    norms = row_norms(Xf) if m == METRIC_L2 else None
+    idx = torch.empty((n, C), dtype=torch.int32, device=Xg.device)
+    dst = torch.empty((n, C), dtype=torch.float32, device=Xg.device)
+    lib = N.lib()
+    with torch.cuda.device(Xg.device):
+        s = N.stream_of(Xg)
+        for r0 in range(0, n, chunk):
+            r1 = min(r0 + chunk, n)
+            for c0 in range(0, n, col_chunk):
+                c1 = min(c0 + col_chunk, n)
+                D = _dots(Xf[r0:r1], Xf[c0:c1], half_exact).contiguous()
+                rc = lib.swb_topc_block(N.ptr(D), r1 - r0, D.shape[1], c1 - c0, r0, c0, N.ptr(norms), m, C,
+                                        N.ptr(idx[r0:r1]), N.ptr(dst[r0:r1]), int(c0 > 0), s)
+                N.check(rc, "knn_candidates")
+                del D
+    return idx, dst
+
+
+@torch.no_grad()
+def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None, metric="ip", protect=None):
+    """Keep a candidate only when no nearer kept neighbour detours to it
+    (swann/build.py:48-91).  Returns int32 [n, deg], -1 padded."""
+    if deg_per_node is not None or protect is not None:
+        raise NotImplementedError("per-node degrees and protected pairs are not part of this build")
+    Xf = Xg.float().contiguous()
+    cand = cand.to(torch.int32).contiguous()
+    cdist = cdist.float().contiguous()
+    n, C = cand.shape
+    out = torch.empty((n, deg), dtype=torch.int32, device=Xg.device)
+    with torch.cuda.device(Xg.device):
+        rc = N.lib().swb_prune(N.ptr(Xf), Xf.shape[0], Xf.shape[1], N.ptr(cand), N.ptr(cdist), n, C, int(deg),
+                               float(alpha), _m(metric), N.ptr(out), N.stream_of(Xg))
+    N.check(rc, "robust_prune")
+    return out
+
+
+@torch.no_grad()
+def add_reverse(Xg, G, deg, chunk=2048, alpha=1.2, max_in=64, deg_per_node=None, metric="ip", rows=None):
+    """Offer every edge back to its target, then re-prune the union per node
+    (swann/build.py:96-150).  rows=(r0, r1) re-prunes only those rows (a
+    rank's block of a sharded build); G is always the whole graph."""
+    if deg_per_node is not None:
+        raise NotImplementedError("per-node degrees are not part of this build")
+    Xf = Xg.float().contiguous()
+    G = G.to(torch.int32).contiguous()
+    n = G.shape[0]
+    r0, r1 = (0, n) if rows is None else rows
+    if G.shape[1] != deg:
+        raise ValueError("add_reverse: the graph's width must equal deg")
+    out = torch.empty((r1 - r0, deg), dtype=torch.int32, device=Xg.device)
+    lib = N.lib()
+    ws_bytes = int(lib.swb_reverse_workspace(n, r1 - r0, G.shape[1], max_in))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=Xg.device)
+    with torch.cuda.device(Xg.device):
+        rc = lib.swb_reverse(N.ptr(Xf), n, Xf.shape[1], N.ptr(G), int(deg), float(alpha), int(max_in), _m(metric),
+                             r0, r1 - r0, N.ptr(out), N.ptr(ws), ws_bytes, N.stream_of(Xg))
+    N.check(rc, "add_reverse")
+    return out
+
+
+@torch.no_grad()
+def build_graph(X, metric: str = "ip", degree: int = 96, candidates: int = 128, alpha: float = 1.2):
+    """Return an (n, degree) int32 neighbour table on the GPU (build.py:156-171)."""
+    if X.device.type != "cuda":
+        X = X.cuda()
+    Xg = X.contiguous()
+    cand, cdist = knn_candidates(Xg, candidates, metric=metric)
+    G = robust_prune(Xg, cand, cdist, degree, alpha=alpha, metric=metric)
+    G = add_reverse(Xg, G, degree, alpha=alpha, metric=metric)
+    return G.to(torch.int32).contiguous()

@@ -1,0 +1,177 @@
+// common.cuh -- device helpers shared by the search and build kernels (sm_100a).
+//
+// Bulk copies: cp.async.bulk (the TMA engine's non-tensor form) moves whole
+// corpus rows from HBM into shared memory and signals an mbarrier with the byte
+// count; one lane issues a row, so a warp keeps many rows in flight without
+// spending registers on them.  Every wait on an mbarrier is bounded.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+namespace swb {
+
+constexpr int NCTR = 10;        // counters per branch (local_search.cu:35-41)
+constexpr int CPROBE = 32;      // probes into the per-query table before giving up
+constexpr int MAXL = 512;       // queue width limit
+constexpr int MAXD = 128;       // graph out-degree limit
+constexpr int MAXV = 128;       // seeds per branch limit
+constexpr int METRIC_IP = 0;
+constexpr int METRIC_L2 = 1;
+constexpr int POLICY_BEST = 0;
+constexpr int POLICY_RR = 1;
+constexpr uint32_t FLT_MAX_BITS = 0x7f7fffffu;
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int ERR_TIMEOUT = 6;  // SWB_ERR_TIMEOUT
+
+// (distance, id) total order (local_search.cu:87-89)
+__device__ __forceinline__ bool key_lt(float da, int ia, float db, int ib) {
+    return (da < db) || (da == db && ia < ib);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy) accesses to the same memory
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar` to complete: gives up after about
+// two seconds of SM clock and returns false (the caller records a status).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (clock64() - t0 > (1ll << 32)) return false;
+    }
+}
+
+__device__ __forceinline__ float ld_volatile_f32(const float* p) {
+    return *reinterpret_cast<const volatile float*>(p);
+}
+
+__device__ __forceinline__ void st_volatile_u64(uint64_t* p, uint64_t v) {
+    *reinterpret_cast<volatile unsigned long long*>(p) = static_cast<unsigned long long>(v);
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// -- distances ------------------------------------------------------------
+//
+// The reference fixes the arithmetic (local_search.cu:185-203, _refcpu.py:21-48):
+// lane l of a TEAM-wide team owns the 16-byte chunks l, l + TEAM, l + 2*TEAM,
+// ... of the row (4 fp32 or 8 fp16 elements each), sums product terms into one
+// fp32 accumulator with the multiply and the add rounded separately, and the
+// team folds its lanes with a shuffle-down tree.  The row arrives here in
+// shared memory instead of straight from HBM; the order is unchanged.
+
+template <typename XT>
+struct VecN;
+template <>
+struct VecN<float> {
+    static constexpr int N = 4;
+};
+template <>
+struct VecN<__half> {
+    static constexpr int N = 8;
+};
+
+__device__ __forceinline__ void widen16(const float* p, float* out) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+}
+__device__ __forceinline__ void widen16(const __half* p, float* out) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+
+template <int TEAM, typename XT>
+__device__ __forceinline__ float team_partial(const float* __restrict__ sq, const XT* __restrict__ row,
+                                              int dim, int metric, int tl) {
+    constexpr int V = VecN<XT>::N;
+    float acc = 0.f;
+    if (metric == METRIC_IP) {
+        for (int base = tl * V; base < dim; base += TEAM * V) {
+            float x[V], q[V];
+            widen16(row + base, x);
+#pragma unroll
+            for (int i = 0; i < V; i += 4) widen16(sq + base + i, q + i);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], x[i]));
+        }
+    } else {
+        for (int base = tl * V; base < dim; base += TEAM * V) {
+            float x[V], q[V];
+            widen16(row + base, x);
+#pragma unroll
+            for (int i = 0; i < V; i += 4) widen16(sq + base + i, q + i);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                const float df = __fsub_rn(q[i], x[i]);
+                acc = __fadd_rn(acc, __fmul_rn(df, df));
+            }
+        }
+    }
+    return acc;
+}
+
+// all 32 lanes call this; each TEAM-wide segment folds independently
+template <int TEAM>
+__device__ __forceinline__ float team_reduce(float acc) {
+#pragma unroll
+    for (int off = TEAM / 2; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(FULL, acc, off, TEAM));
+    return acc;
+}
+
+}  // namespace swb

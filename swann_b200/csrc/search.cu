@@ -1,0 +1,1119 @@
+// search.cu -- multi-branch graph search for sm_100a.
+//
+// Replaces the reference's init_kernel / advance_kernel / merge_branches_kernel
+// (swann/csrc/local_search.cu:271-919).  Same semantics, different machine
+// mapping:
+//
+//  * one WARP per branch (the reference spends a 128-thread CTA).  Selection,
+//    compaction, sorting and the queue merge are warp-synchronous (ballots and
+//    shuffles, no __syncthreads), and all D neighbours of an expansion probe the
+//    shared table at once, one lane per neighbour;
+//  * neighbour rows are gathered by bulk copies (cp.async.bulk) into a per-warp
+//    ring of shared-memory rows, so a warp has several whole rows in flight
+//    while its teams reduce the ones that have landed;
+//  * the per-query distance table packs (id + 1, distance bits) into one
+//    64-bit word: one compare-and-swap claims a node or returns its distance;
+//  * Index.search runs as one fused kernel: init, the walk for the whole
+//    budget, each branch's best kk, and -- in the last branch of a query to
+//    finish -- the merge of that query's branches.
+//
+// The distance arithmetic is the reference's, bit for bit (common.cuh).
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace swb {
+
+// ---------------------------------------------------------------------------
+// launch knobs and the per-warp shared-memory carve-up
+
+struct Knobs {
+    const void* X;
+    int64_t n;
+    int dim, rowbytes;
+    const int32_t* G;
+    int D;
+    const float* Qv;
+    const int32_t* seeds;
+    int32_t* ids;
+    float* dist;
+    uint8_t* expd;
+    uint8_t* lin;
+    int Q, J, L, V;
+    int32_t* visited;
+    int H;
+    int32_t* counters;
+    int metric, delta, max_exp, policy;
+    float stop_eps;
+    int kstop;
+    uint64_t* cache;
+    int Hc;
+    float* bound;
+    int exclusive, stall_patience;
+    float crowd_frac;
+    const int32_t* active;
+    int n_active;
+    int32_t* status;
+    int k, kk;
+    int32_t* branch_ids;
+    float* branch_dist;
+    int32_t* qdone;
+    int32_t* out_ids;
+    float* out_dist;
+    int W, R, warp_bytes, q_shared;
+};
+
+__host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
+
+struct Layout {
+    int q, ring, mbar, s_id, s_d, s_e, s_l, n_id, n_d, n_e, n_l, c_id, c_d, c_l, w_v, w_slot, w_d, w_aux,
+        retired, total;
+};
+
+// q_bytes = 0 when the query lives once per CTA rather than per warp
+__host__ __device__ inline Layout warp_layout(int L, int R, int rowbytes, int q_bytes) {
+    Layout w;
+    int o = 0;
+    w.ring = o; o += R * rowbytes;      // 16-byte multiples: first, so rows stay aligned
+    w.q = o; o += align16(q_bytes);
+    w.mbar = o; o += align16(R * 8);
+    w.s_id = o; o += align16(L * 4);
+    w.s_d = o; o += align16(L * 4);
+    w.n_id = o; o += align16(L * 4);
+    w.n_d = o; o += align16(L * 4);
+    w.s_e = o; o += align16(L);
+    w.s_l = o; o += align16(L);
+    w.n_e = o; o += align16(L);
+    w.n_l = o; o += align16(L);
+    w.c_id = o; o += MAXD * 4;
+    w.c_d = o; o += MAXD * 4;
+    w.c_l = o; o += MAXD;
+    w.w_v = o; o += MAXD * 4;
+    w.w_slot = o; o += MAXD * 4;
+    w.w_d = o; o += MAXD * 4;
+    w.w_aux = o; o += MAXD * 4;
+    w.retired = o; o += 32;
+    w.total = align16(o);
+    return w;
+}
+
+struct WarpMem {
+    float* q;
+    char* ring;
+    uint64_t* mbar;
+    int* s_id;
+    float* s_d;
+    uint8_t* s_e;
+    uint8_t* s_l;
+    int* n_id;
+    float* n_d;
+    uint8_t* n_e;
+    uint8_t* n_l;
+    int* c_id;
+    float* c_d;
+    uint8_t* c_l;
+    int* w_v;
+    int* w_slot;
+    float* w_d;
+    int* w_aux;
+    uint32_t* retired;
+};
+
+__device__ inline WarpMem carve(char* base, const Layout& l) {
+    WarpMem w;
+    w.ring = base + l.ring;
+    w.q = reinterpret_cast<float*>(base + l.q);
+    w.mbar = reinterpret_cast<uint64_t*>(base + l.mbar);
+    w.s_id = reinterpret_cast<int*>(base + l.s_id);
+    w.s_d = reinterpret_cast<float*>(base + l.s_d);
+    w.n_id = reinterpret_cast<int*>(base + l.n_id);
+    w.n_d = reinterpret_cast<float*>(base + l.n_d);
+    w.s_e = reinterpret_cast<uint8_t*>(base + l.s_e);
+    w.s_l = reinterpret_cast<uint8_t*>(base + l.s_l);
+    w.n_e = reinterpret_cast<uint8_t*>(base + l.n_e);
+    w.n_l = reinterpret_cast<uint8_t*>(base + l.n_l);
+    w.c_id = reinterpret_cast<int*>(base + l.c_id);
+    w.c_d = reinterpret_cast<float*>(base + l.c_d);
+    w.c_l = reinterpret_cast<uint8_t*>(base + l.c_l);
+    w.w_v = reinterpret_cast<int*>(base + l.w_v);
+    w.w_slot = reinterpret_cast<int*>(base + l.w_slot);
+    w.w_d = reinterpret_cast<float*>(base + l.w_d);
+    w.w_aux = reinterpret_cast<int*>(base + l.w_aux);
+    w.retired = reinterpret_cast<uint32_t*>(base + l.retired);
+    return w;
+}
+
+// ---------------------------------------------------------------------------
+// hashing (local_search.cu:94-110, 169-183)
+
+__device__ __forceinline__ uint32_t knuth(int key, uint32_t mask) { return (2654435761u * (uint32_t)key) & mask; }
+
+// Per-branch visited set: int slots holding id + 1.  Returns 1 when this call
+// inserted `v`; a full table sets `fail` and reports "not new".
+__device__ __forceinline__ int visited_insert(int* tab, int H, int v, int& fail) {
+    const uint32_t mask = (uint32_t)(H - 1);
+    uint32_t pos = knuth(v, mask);
+    for (int p = 0; p < H; ++p) {
+        const int old = atomicCAS(&tab[pos], 0, v + 1);
+        if (old == 0) return 1;
+        if (old == v + 1) return 0;
+        pos = (pos + 1) & mask;
+    }
+    fail = 1;
+    return 0;
+}
+
+// Per-query distance table slot = (id + 1) << 32 | float bits; a claimed but
+// not yet scored slot carries FLT_MAX.  Returns the cached distance (FLT_MAX
+// when none), the slot (-1 after CPROBE probes) and whether this call claimed it.
+__device__ __forceinline__ float cache_probe(uint64_t* tab, int Hc, int v, int& slot, int& claimed) {
+    const uint32_t mask = (uint32_t)(Hc - 1);
+    uint32_t pos = knuth(v, mask);
+    const uint32_t key = (uint32_t)(v + 1);
+    const unsigned long long want = ((unsigned long long)key << 32) | FLT_MAX_BITS;
+    for (int p = 0; p < CPROBE; ++p) {
+        const unsigned long long old = atomicCAS(reinterpret_cast<unsigned long long*>(&tab[pos]), 0ull, want);
+        if (old == 0ull) {
+            slot = (int)pos;
+            claimed = 1;
+            return FLT_MAX;
+        }
+        if ((uint32_t)(old >> 32) == key) {
+            slot = (int)pos;
+            claimed = 0;
+            return __uint_as_float((uint32_t)old);
+        }
+        pos = (pos + 1) & mask;
+    }
+    slot = -1;
+    claimed = 0;
+    return FLT_MAX;
+}
+
+__device__ __forceinline__ uint64_t cache_pack(int v, float d) {
+    return ((uint64_t)(uint32_t)(v + 1) << 32) | (uint64_t)__float_as_uint(d);
+}
+
+// ---------------------------------------------------------------------------
+// distances for a list of rows: w.w_v[0..m) -> w.w_d[0..m)
+
+struct Ring {
+    uint32_t phases;   // parity of the next wait, one bit per slot
+};
+
+template <typename XT>
+__device__ __forceinline__ void issue_row(const Knobs& K, const WarpMem& w, int item) {
+    const int s = item % K.R;
+    const int v = w.w_v[item];
+    const char* src = reinterpret_cast<const char*>(K.X) + (size_t)v * (size_t)K.rowbytes;
+    fence_proxy_async_smem();
+    mbar_expect_tx(&w.mbar[s], (uint32_t)K.rowbytes);
+    bulk_g2s(w.ring + (size_t)s * K.rowbytes, src, (uint32_t)K.rowbytes, &w.mbar[s]);
+}
+
+// Scores the m rows listed in w.w_v with TEAM-lane teams, 32/TEAM rows at a
+// time, while later rows stream into the ring.  Rows with w.w_slot >= 0 are
+// published to the per-query table `ctab` as soon as they are scored.
+// Returns false (after draining the copies in flight) if a wait ran out.
+template <int TEAM, typename XT>
+__device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, const float* sq,
+                           uint64_t* ctab, int lane) {
+    if (m == 0) return true;
+    constexpr int P = 32 / TEAM;
+    const int R = K.R;
+    const int team = lane / TEAM, tl = lane % TEAM;
+    const int first = m < R ? m : R;
+    if (lane < first) issue_row<XT>(K, w, lane);
+    // Items [base, min(m, base + R)) are in flight at the top of each round,
+    // one per slot.
+    for (int base = 0; base < m; base += P) {
+        const int i = base + team;
+        float acc = 0.f;
+        bool good = true;
+        if (i < m) {
+            const int s = i % R;
+            good = mbar_wait(&w.mbar[s], (ring.phases >> s) & 1u);
+            if (good)
+                acc = team_partial<TEAM, XT>(sq, reinterpret_cast<const XT*>(w.ring + (size_t)s * K.rowbytes),
+                                             K.dim, K.metric, tl);
+        }
+        acc = team_reduce<TEAM>(acc);
+        if (tl == 0 && i < m && good) {
+            const float d = (K.metric == METRIC_IP) ? __fsub_rn(1.f, acc) : acc;
+            w.w_d[i] = d;
+            const int slot = w.w_slot[i];
+            if (slot >= 0) st_volatile_u64(&ctab[slot], cache_pack(w.w_v[i], d));
+        }
+        // a slot's parity advances only when its wait succeeded
+        const unsigned goodmask = __ballot_sync(FULL, good);
+#pragma unroll
+        for (int t = 0; t < P; ++t) {
+            const int ii = base + t;
+            if (ii < m && ((goodmask >> (t * TEAM)) & 1u)) ring.phases ^= 1u << (ii % R);
+        }
+        if (goodmask != FULL) {
+            // A wait ran out.  Record it, then wait (bounded) for every copy
+            // still in flight before the shared memory can be released.
+            const int end = min(m, base + R);
+            for (int ii = base; ii < end; ++ii) {
+                const int t = ii - base;
+                if (t < P && ((goodmask >> (t * TEAM)) & 1u)) continue;
+                const int s = ii % R;
+                if (lane == 0) mbar_wait(&w.mbar[s], (ring.phases >> s) & 1u);
+                ring.phases ^= 1u << s;
+            }
+            if (lane == 0 && K.status) atomicExch(K.status, ERR_TIMEOUT);
+            __syncwarp();
+            return false;
+        }
+        __syncwarp();
+        if (lane < P) {
+            const int ni = base + lane + R;
+            if (ni < m) issue_row<XT>(K, w, ni);
+        }
+    }
+    __syncwarp();
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// sorting
+
+// 32 keys, one per lane, ascending by (d, id); lineage rides along
+__device__ __forceinline__ void warp_sort32(float& d, int& id, int& l, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float pd = __shfl_xor_sync(FULL, d, j);
+            const int pid = __shfl_xor_sync(FULL, id, j);
+            const int pl = __shfl_xor_sync(FULL, l, j);
+            const bool up = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            const bool take = (lower == up) ? key_lt(pd, pid, d, id) : key_lt(d, id, pd, pid);
+            if (take) {
+                d = pd;
+                id = pid;
+                l = pl;
+            }
+        }
+    }
+}
+
+// n (a power of two, <= 128) keys in shared memory, ascending; warp-synchronous
+__device__ void smem_sort(int* cid, float* cd, uint8_t* cl, int n, int lane) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < n; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const bool asc = (i & k) == 0;
+                    const bool need = asc ? key_lt(cd[ixj], cid[ixj], cd[i], cid[i])
+                                          : key_lt(cd[i], cid[i], cd[ixj], cid[ixj]);
+                    if (need) {
+                        const float td = cd[i]; cd[i] = cd[ixj]; cd[ixj] = td;
+                        const int ti = cid[i]; cid[i] = cid[ixj]; cid[ixj] = ti;
+                        if (cl) { const uint8_t tl = cl[i]; cl[i] = cl[ixj]; cl[ixj] = tl; }
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// one branch
+
+__device__ __forceinline__ bool is_retired(const WarpMem& w, unsigned li) {
+    return (w.retired[li >> 5] >> (li & 31)) & 1u;
+}
+__device__ __forceinline__ void set_retired(const WarpMem& w, unsigned li, int lane) {
+    if (lane == 0) w.retired[li >> 5] |= (1u << (li & 31));
+    __syncwarp();
+}
+
+// The selection of local_search.cu:453-511, one ballot per 32 queue slots.
+__device__ int select_slot(const Knobs& K, const WarpMem& w, int lane, int ctr0, float limit, bool early) {
+    const int L = K.L;
+    if (K.policy == POLICY_RR && K.V > 1) {
+        int slot = -1;
+        for (int turn = 0; turn < K.V && slot < 0; ++turn) {
+            const int want = (ctr0 + turn) % K.V;
+            if (is_retired(w, (unsigned)want)) continue;
+            int found = -1;
+            for (int b = 0; b < L && found < 0; b += 32) {
+                const int i = b + lane;
+                const bool c = i < L && w.s_id[i] >= 0 && w.s_e[i] == 0 && w.s_l[i] == want;
+                const unsigned msk = __ballot_sync(FULL, c);
+                if (msk) found = b + __ffs(msk) - 1;
+            }
+            if (found < 0 || (early && w.s_d[found] > limit)) {
+                set_retired(w, (unsigned)want, lane);
+                continue;
+            }
+            slot = found;
+        }
+        if (slot < 0 && !early) {
+            for (int b = 0; b < L; b += 32) {
+                const int i = b + lane;
+                const unsigned msk = __ballot_sync(FULL, i < L && w.s_id[i] >= 0 && w.s_e[i] == 0);
+                if (msk) return b + __ffs(msk) - 1;
+            }
+        }
+        return slot;
+    }
+    for (int b = 0; b < L; b += 32) {
+        const int i = b + lane;
+        bool c = false;
+        if (i < L && w.s_id[i] >= 0 && w.s_e[i] == 0) c = !is_retired(w, w.s_l[i]);
+        const unsigned msk = __ballot_sync(FULL, c);
+        if (msk) {
+            const int f = b + __ffs(msk) - 1;
+            return (!early || w.s_d[f] <= limit) ? f : -1;
+        }
+    }
+    return -1;
+}
+
+// Merge the nk sorted candidates in c_* into the queue s_* -> n_*, one output
+// slot per lane at a time, by the merge-path rule of local_search.cu:637-650
+// (ties between a queue entry and a candidate resolve exactly as there).
+__device__ void merge_queue(const WarpMem& w, int L, int nk, int lane) {
+    for (int o = lane; o < L; o += 32) {
+        int lo = max(0, o - nk), hi = min(o, L);
+        while (lo < hi) {
+            const int i = (lo + hi) >> 1, j = o - i;
+            if (j > 0 && !key_lt(w.c_d[j - 1], w.c_id[j - 1], w.s_d[i], w.s_id[i])) lo = i + 1;
+            else hi = i;
+        }
+        const int i = lo, j = o - i;
+        const bool takeA = (j >= nk) || (i < L && key_lt(w.s_d[i], w.s_id[i], w.c_d[j], w.c_id[j]));
+        int id;
+        float d;
+        uint8_t e, l;
+        if (takeA) { id = w.s_id[i]; d = w.s_d[i]; e = w.s_e[i]; l = w.s_l[i]; }
+        else { id = w.c_id[j]; d = w.c_d[j]; e = 0; l = w.c_l[j]; }
+        if (id < 0) { d = FLT_MAX; e = 1; l = 0; }
+        w.n_id[o] = id; w.n_d[o] = d; w.n_e[o] = e; w.n_l[o] = l;
+    }
+}
+
+__device__ __forceinline__ void swap_queue(WarpMem& w) {
+    int* ti = w.s_id; w.s_id = w.n_id; w.n_id = ti;
+    float* td = w.s_d; w.s_d = w.n_d; w.n_d = td;
+    uint8_t* te = w.s_e; w.s_e = w.n_e; w.n_e = te;
+    uint8_t* tl = w.s_l; w.s_l = w.n_l; w.n_l = tl;
+}
+
+// Seeds -> sorted queue (local_search.cu:318-350).  Duplicate seeds keep their
+// first occurrence (the CPU reference's rule, _refcpu.py:68-74).
+template <int TEAM, typename XT>
+__device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring,
+                            int* ctr) {
+    int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
+    if (vis) {
+        if (K.H >= 128) {
+            int4* v4 = reinterpret_cast<int4*>(vis);
+            for (int t = lane; t < K.H / 4; t += 32) v4[t] = make_int4(0, 0, 0, 0);
+        } else {
+            for (int t = lane; t < K.H; t += 32) vis[t] = 0;
+        }
+    }
+    for (int c = 0; c < NCTR; ++c) ctr[c] = 0;
+    const int V = K.V;
+    int nsort = 2;
+    while (nsort < V && nsort < MAXV) nsort <<= 1;
+    for (int i = lane; i < nsort; i += 32) { w.c_id[i] = -1; w.c_d[i] = FLT_MAX; w.c_l[i] = 0; }
+    __syncwarp();   // the clears above are ordered before the inserts below
+    const int32_t* sd = K.seeds + ((size_t)q * K.J + j) * (size_t)V;
+    int m = 0, fails = 0;
+    for (int b = 0; b < V; b += 32) {
+        const int i = b + lane;
+        int s = (i < V) ? sd[i] : -1;
+        if (s >= K.n) s = -1;   // an id outside the corpus is an empty slot
+        bool use = s >= 0;
+        for (int jj = 0; use && jj < i; ++jj) use = (sd[jj] != s);
+        if (use && vis) {
+            int fail = 0;
+            use = visited_insert(vis, K.H, s, fail) != 0;
+            fails += fail;
+        }
+        const unsigned msk = __ballot_sync(FULL, use);
+        if (use) {
+            const int pos = m + __popc(msk & lanemask_lt());
+            w.w_v[pos] = s;
+            w.w_slot[pos] = -1;
+            w.w_aux[pos] = i;
+        }
+        m += __popc(msk);
+    }
+    for (int off = 16; off > 0; off >>= 1) fails += __shfl_xor_sync(FULL, fails, off);
+    __syncwarp();
+    score_rows<TEAM, XT>(K, w, m, ring, sq, nullptr, lane);
+    ctr[1] += m;
+    ctr[2] += fails;
+    for (int t = lane; t < m; t += 32) {
+        const int si = w.w_aux[t];
+        w.c_id[si] = w.w_v[t];
+        w.c_d[si] = w.w_d[t];
+        w.c_l[si] = (uint8_t)si;
+    }
+    __syncwarp();
+    smem_sort(w.c_id, w.c_d, w.c_l, nsort, lane);
+    for (int i = lane; i < K.L; i += 32) {
+        const bool ok = (i < nsort) && (w.c_id[i] >= 0);
+        w.s_id[i] = ok ? w.c_id[i] : -1;
+        w.s_d[i] = ok ? w.c_d[i] : FLT_MAX;
+        w.s_e[i] = ok ? 0 : 1;
+        w.s_l[i] = ok ? w.c_l[i] : 0;
+    }
+    __syncwarp();
+}
+
+// The walk: up to `delta` expansions (local_search.cu:451-683).
+template <int TEAM, typename XT>
+__device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring, int* ctr,
+                     int delta) {
+    int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
+    uint64_t* ctab = (K.Hc > 0) ? K.cache + (size_t)q * (size_t)K.Hc : nullptr;
+    float* bnd = K.bound ? K.bound + q : nullptr;
+    const int L = K.L, D = K.D;
+    const int kr = K.kstop < L ? K.kstop : L;
+    const bool early = K.stop_eps >= 0.f;
+    const float one_eps = __fadd_rn(1.f, K.stop_eps);
+    float best_k = FLT_MAX;
+    int stall = 0, crowd_run = 0;
+    if (lane < 8) w.retired[lane] = 0u;
+    __syncwarp();
+
+    for (int step = 0; step < delta; ++step) {
+        if (ctr[0] >= K.max_exp) break;
+        float radius = (kr > 0 && w.s_id[kr - 1] >= 0) ? w.s_d[kr - 1] : FLT_MAX;
+        if (bnd) {
+            float gb = 0.f;
+            if (lane == 0) gb = ld_volatile_f32(bnd);
+            gb = __shfl_sync(FULL, gb, 0);
+            if (gb < radius) radius = gb;
+        }
+        const float limit = (radius == FLT_MAX) ? FLT_MAX : __fmul_rn(radius, one_eps);
+        const int slot = select_slot(K, w, lane, ctr[0], limit, early);
+        if (slot < 0) {
+            ctr[3] = 1;
+            break;
+        }
+        const int p = w.s_id[slot];
+        const int plin = w.s_l[slot];
+        __syncwarp();
+        if (lane == 0) w.s_e[slot] = 1;
+        ctr[0] += 1;
+
+        // -- expand p: one lane per neighbour slot ------------------------
+        int nv[4], nst[4], nsl[4];
+        float nd[4];
+        int cov = 0, nbr = 0, fails = 0, hits = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int nidx = lane + 32 * t;
+            int v = (nidx < D) ? __ldg(&K.G[(size_t)p * D + nidx]) : -1;
+            if (v >= K.n) v = -1;   // an edge outside the corpus is no edge
+            nv[t] = v;
+            nst[t] = 0;   // 0 none, 1 candidate with distance, 2 to be scored
+            nsl[t] = -1;
+            nd[t] = FLT_MAX;
+            if (v >= 0) {
+                ++nbr;
+                int isnew = 1, fail = 0;
+                if (vis) isnew = visited_insert(vis, K.H, v, fail);
+                fails += fail;
+                if (!isnew) {
+                    ++cov;
+                } else {
+                    int cslot = -1, claimed = 0;
+                    float d = FLT_MAX;
+                    if (ctab) d = cache_probe(ctab, K.Hc, v, cslot, claimed);
+                    const bool taken = K.exclusive && cslot >= 0 && !claimed && d != FLT_MAX;
+                    if (taken) {
+                        ++hits;
+                        ++cov;
+                    } else if (d == FLT_MAX) {
+                        nst[t] = 2;
+                        nsl[t] = cslot;
+                    } else {
+                        ++hits;
+                        nst[t] = 1;
+                        nd[t] = d;
+                    }
+                }
+            }
+        }
+        // rows to score, compacted in slot order
+        int m = 0, pos[4], claimed_rows = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const unsigned msk = __ballot_sync(FULL, nst[t] == 2);
+            pos[t] = m + __popc(msk & lanemask_lt());
+            if (nst[t] == 2) {
+                w.w_v[pos[t]] = nv[t];
+                w.w_slot[pos[t]] = nsl[t];
+            }
+            m += __popc(msk);
+            claimed_rows += __popc(__ballot_sync(FULL, nst[t] == 2 && nsl[t] >= 0));
+        }
+        __syncwarp();
+        if (!score_rows<TEAM, XT>(K, w, m, ring, sq, ctab, lane)) break;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            if (nst[t] == 2) {
+                nd[t] = w.w_d[pos[t]];
+                nst[t] = 1;
+            }
+        for (int off = 16; off > 0; off >>= 1) {
+            cov += __shfl_xor_sync(FULL, cov, off);
+            nbr += __shfl_xor_sync(FULL, nbr, off);
+            fails += __shfl_xor_sync(FULL, fails, off);
+            hits += __shfl_xor_sync(FULL, hits, off);
+        }
+        ctr[1] += m;
+        ctr[2] += fails;
+        ctr[4] += hits;
+        ctr[5] += claimed_rows;
+
+        // -- keep what can still enter the queue, sort it, merge ------------
+        const float worst = (w.s_id[L - 1] >= 0) ? w.s_d[L - 1] : FLT_MAX;
+        int nk = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const bool keep = nst[t] == 1 && (worst == FLT_MAX || nd[t] <= worst);
+            const unsigned msk = __ballot_sync(FULL, keep);
+            if (keep) {
+                const int ps = nk + __popc(msk & lanemask_lt());
+                w.c_id[ps] = nv[t];
+                w.c_d[ps] = nd[t];
+                w.c_l[ps] = (uint8_t)plin;
+            }
+            nk += __popc(msk);
+        }
+        ctr[8] += nk;
+        ctr[9] += 1;
+        __syncwarp();
+        if (nk > 0) {
+            if (nk <= 32) {
+                float d = (lane < nk) ? w.c_d[lane] : __int_as_float(0x7f800000);
+                int id = (lane < nk) ? w.c_id[lane] : 0x7fffffff;
+                int l = plin;
+                warp_sort32(d, id, l, lane);
+                __syncwarp();
+                if (lane < nk) { w.c_d[lane] = d; w.c_id[lane] = id; w.c_l[lane] = (uint8_t)l; }
+            } else {
+                int ms = 2;
+                while (ms < nk) ms <<= 1;
+                for (int i = nk + lane; i < ms; i += 32) {
+                    w.c_d[i] = __int_as_float(0x7f800000);
+                    w.c_id[i] = 0x7fffffff;
+                    w.c_l[i] = 0;
+                }
+                __syncwarp();
+                smem_sort(w.c_id, w.c_d, w.c_l, ms, lane);
+            }
+            __syncwarp();
+            merge_queue(w, L, nk, lane);
+            __syncwarp();
+            swap_queue(w);
+        }
+        if (bnd && lane == 0 && kr > 0 && w.s_id[kr - 1] >= 0)
+            atomicMin(reinterpret_cast<int*>(bnd), __float_as_int(w.s_d[kr - 1]));
+        if (K.crowd_frac > 0.f) {
+            const float cv = (nbr > 0) ? __fdiv_rn((float)cov, (float)nbr) : 0.f;
+            if (cv >= K.crowd_frac) {
+                if (++crowd_run >= 2) {
+                    set_retired(w, (unsigned)plin, lane);
+                    ctr[7] += 1;
+                    crowd_run = 0;
+                }
+            } else {
+                crowd_run = 0;
+            }
+        }
+        if (K.stall_patience > 0) {
+            const float bk = (kr > 0 && w.s_id[kr - 1] >= 0) ? w.s_d[kr - 1] : FLT_MAX;
+            if (bk < best_k) { best_k = bk; stall = 0; }
+            else stall += 1;
+            if (stall >= K.stall_patience) {
+                ctr[6] = 1;
+                break;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// per-warp set-up and state transfer
+
+__device__ __forceinline__ void ring_setup(const Knobs& K, WarpMem& w, int lane, Ring& ring) {
+    if (lane == 0) {
+        for (int s = 0; s < K.R; ++s) mbar_init(&w.mbar[s], 1);
+        fence_mbar_init();
+        fence_proxy_async_smem();
+    }
+    ring.phases = 0u;
+    __syncwarp();
+}
+
+__device__ __forceinline__ void load_query(float* sq, const float* src, int dim, int tid, int nthreads) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(sq);
+    for (int t = tid; t < dim / 4; t += nthreads) d4[t] = __ldg(&s4[t]);
+}
+
+__device__ void load_state(const Knobs& K, WarpMem& w, size_t bid, int lane, int* ctr) {
+    const size_t o = bid * (size_t)K.L;
+    for (int i = lane; i < K.L; i += 32) {
+        w.s_id[i] = K.ids[o + i];
+        w.s_d[i] = K.dist[o + i];
+        w.s_e[i] = K.expd[o + i];
+        w.s_l[i] = K.lin[o + i];
+    }
+    for (int c = 0; c < NCTR; ++c) ctr[c] = K.counters[bid * NCTR + c];
+    __syncwarp();
+}
+
+__device__ void store_state(const Knobs& K, const WarpMem& w, size_t bid, int lane, const int* ctr) {
+    if (K.ids) {
+        const size_t o = bid * (size_t)K.L;
+        for (int i = lane; i < K.L; i += 32) {
+            K.ids[o + i] = w.s_id[i];
+            K.dist[o + i] = w.s_d[i];
+            K.expd[o + i] = w.s_e[i];
+            K.lin[o + i] = w.s_l[i];
+        }
+    }
+    if (K.counters && lane < NCTR) {
+        int v = ctr[0];
+#pragma unroll
+        for (int c = 1; c < NCTR; ++c)
+            if (lane == c) v = ctr[c];
+        K.counters[bid * NCTR + lane] = v;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// kernels
+
+template <int TEAM, typename XT>
+__global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs K) {
+    extern __shared__ __align__(128) char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = blockIdx.x * K.W + warp;
+    if (g >= K.Q * K.J) return;
+    const int q = g / K.J, j = g % K.J;
+    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4);
+    WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
+    Ring ring;
+    ring_setup(K, w, lane, ring);
+    load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
+    // the per-query table and bound belong to the query; its J branches clear
+    // them between them (local_search.cu:302-313)
+    if (K.Hc > 0) {
+        uint4* c4 = reinterpret_cast<uint4*>(K.cache + (size_t)q * K.Hc);
+        const int n4 = K.Hc / 2;
+        for (int t = j * 32 + lane; t < n4; t += K.J * 32) c4[t] = make_uint4(0, 0, 0, 0);
+        if (K.Hc == 1 && j == 0 && lane == 0) K.cache[q] = 0ull;
+    }
+    if (K.bound && j == 0 && lane == 0) K.bound[q] = FLT_MAX;
+    __syncwarp();
+    int ctr[NCTR];
+    init_branch<TEAM, XT>(K, w, q, j, lane, w.q, ring, ctr);
+    store_state(K, w, (size_t)q * K.J + j, lane, ctr);
+}
+
+template <int TEAM, typename XT>
+__global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Knobs K) {
+    extern __shared__ __align__(128) char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = blockIdx.x * K.W + warp;
+    int flat;
+    if (K.active) {
+        if (g >= K.n_active) return;
+        flat = K.active[g];
+    } else {
+        if (g >= K.Q * K.J) return;
+        flat = g;
+    }
+    const int q = flat / K.J, j = flat % K.J;
+    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4);
+    WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
+    Ring ring;
+    ring_setup(K, w, lane, ring);
+    load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
+    int ctr[NCTR];
+    load_state(K, w, (size_t)flat, lane, ctr);
+    walk<TEAM, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
+    __syncwarp();
+    store_state(K, w, (size_t)flat, lane, ctr);
+}
+
+// k nearest unique ids over J sorted branch lists of kk (distance, id) pairs:
+// a J-way merge whose heads the warp scans with one ballot-free argmin per
+// output.  Copies of an id carry identical distances, so they come out
+// consecutively and all but the first are skipped.
+__device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, int kk, int k, int* head,
+                                   int32_t* oi, float* od, int lane) {
+    for (int t = lane; t < J; t += 32) head[t] = 0;
+    __syncwarp();
+    int w = 0, last = -1;
+    while (w < k) {
+        float bdv = __int_as_float(0x7f800000);
+        int bid = 0x7fffffff, bj = -1;
+        for (int t = lane; t < J; t += 32) {
+            const int h = head[t];
+            if (h < kk) {
+                const int id = __ldcg(&bi[t * kk + h]);
+                const float d = (id >= 0) ? __ldcg(&bd[t * kk + h]) : __int_as_float(0x7f800000);
+                const int idk = (id >= 0) ? id : 0x7fffffff;
+                if (key_lt(d, idk, bdv, bid)) { bdv = d; bid = idk; bj = t; }
+            }
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            const float pd = __shfl_xor_sync(FULL, bdv, off);
+            const int pid = __shfl_xor_sync(FULL, bid, off);
+            const int pj = __shfl_xor_sync(FULL, bj, off);
+            if (key_lt(pd, pid, bdv, bid) || (pd == bdv && pid == bid && pj >= 0 && (bj < 0 || pj < bj))) {
+                bdv = pd; bid = pid; bj = pj;
+            }
+        }
+        if (bj < 0 || bid == 0x7fffffff) break;
+        if (lane == 0) head[bj] += 1;
+        __syncwarp();
+        if (bid != last) {
+            if (lane == 0) { oi[w] = bid; od[w] = bdv; }
+            ++w;
+            last = bid;
+        }
+    }
+    for (int t = w + lane; t < k; t += 32) { oi[t] = -1; od[t] = __int_as_float(0x7f800000); }
+}
+
+template <int TEAM, typename XT>
+__global__ void __launch_bounds__(256) fused_kernel(const __grid_constant__ Knobs K) {
+    extern __shared__ __align__(128) char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.y;
+    const int j = blockIdx.x * K.W + warp;
+    float* sq = reinterpret_cast<float*>(smem);
+    const int qbytes = align16(K.dim * 4);
+    load_query(sq, K.Qv + (size_t)q * K.dim, K.dim, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (j >= K.J) return;
+    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, 0);
+    WarpMem w = carve(smem + qbytes + (size_t)warp * K.warp_bytes, lay);
+    Ring ring;
+    ring_setup(K, w, lane, ring);
+    int ctr[NCTR];
+    init_branch<TEAM, XT>(K, w, q, j, lane, sq, ring, ctr);
+    walk<TEAM, XT>(K, w, q, j, lane, sq, ring, ctr, K.max_exp);
+    __syncwarp();
+    const size_t bid = (size_t)q * K.J + j;
+    store_state(K, w, bid, lane, ctr);
+    for (int t = lane; t < K.kk; t += 32) {
+        K.branch_ids[bid * K.kk + t] = w.s_id[t];
+        K.branch_dist[bid * K.kk + t] = w.s_d[t];
+    }
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(&K.qdone[q], 1) == K.J - 1);
+    last = __shfl_sync(FULL, last, 0);
+    if (!last) return;
+    __threadfence();
+    // the walk is over: w_v .. w_aux (4 * MAXD ints, contiguous) hold the heads
+    merge_sorted_lists(K.branch_ids + (size_t)q * K.J * K.kk, K.branch_dist + (size_t)q * K.J * K.kk, K.J, K.kk,
+                       K.k, w.w_v, K.out_ids + (size_t)q * K.k, K.out_dist + (size_t)q * K.k, lane);
+}
+
+__global__ void prepare_kernel(int Q, uint64_t* cache, int64_t cache_words, float* bound, int32_t* qdone) {
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (cache) {
+        uint4* c4 = reinterpret_cast<uint4*>(cache);
+        for (int64_t t = tid; t < cache_words / 2; t += stride) c4[t] = make_uint4(0, 0, 0, 0);
+        if ((cache_words & 1) && tid == 0) cache[cache_words - 1] = 0ull;
+    }
+    for (int64_t t = tid; t < Q; t += stride) {
+        if (bound) bound[t] = FLT_MAX;
+        if (qdone) qdone[t] = 0;
+    }
+}
+
+// Standalone merge (local_search.cu:863-919): any [Q, J, kk] input; one block
+// per query sorts the padded set by (distance, id) and keeps the first copy
+// of each id.
+__global__ void __launch_bounds__(256) merge_kernel(const int32_t* __restrict__ bi, const float* __restrict__ bd,
+                                                    int n, int k, int padded, int32_t* oi, float* od) {
+    extern __shared__ __align__(128) char smem[];
+    float* sd = reinterpret_cast<float*>(smem);
+    int* si = reinterpret_cast<int*>(sd + padded);
+    const int q = blockIdx.x;
+    const size_t base = (size_t)q * n;
+    for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+        const int id = (i < n) ? bi[base + i] : -1;
+        si[i] = (id >= 0) ? id : 0x7fffffff;
+        sd[i] = (id >= 0) ? bd[base + i] : __int_as_float(0x7f800000);
+    }
+    __syncthreads();
+    for (int size = 2; size <= padded; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < padded; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool up = (i & size) == 0;
+                    const bool lt = key_lt(sd[i], si[i], sd[j], si[j]);
+                    if (up != lt) {
+                        const float td = sd[i]; sd[i] = sd[j]; sd[j] = td;
+                        const int ti = si[i]; si[i] = si[j]; si[j] = ti;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0) {
+        int w = 0;
+        for (int i = 0; i < n && w < k; ++i) {
+            if (si[i] == 0x7fffffff) break;
+            if (i > 0 && si[i] == si[i - 1]) continue;
+            oi[(size_t)q * k + w] = si[i];
+            od[(size_t)q * k + w] = sd[i];
+            ++w;
+        }
+        for (; w < k; ++w) {
+            oi[(size_t)q * k + w] = -1;
+            od[(size_t)q * k + w] = __int_as_float(0x7f800000);
+        }
+    }
+}
+
+}  // namespace swb
+
+// ===========================================================================
+// host side
+
+using namespace swb;
+
+namespace {
+
+int esize_of(int x_dtype) { return x_dtype == 0 ? 4 : 2; }
+
+int pick_ring(int rowbytes, int team) {
+    // Rows in flight per warp: a staging budget per warp, at least the rows
+    // one round scores (32 / team), at most 32 (one issuing lane each).
+    int budget = abi::env_int("SWB_RING_BYTES", 12 * 1024);
+    int r = budget / rowbytes;
+    const int p = 32 / team;
+    if (r < p) r = p;
+    if (r < 2) r = 2;
+    if (r > 32) r = 32;
+    return r;
+}
+
+int common_checks(const void* X, int x_dtype, int64_t n, int dim, int team, int L) {
+    if (!X) return abi::fail(SWB_ERR_ARG, "X is null");
+    if (x_dtype != SWB_F32 && x_dtype != SWB_F16) return abi::fail(SWB_ERR_ARG, "X must be float32 or float16");
+    if (n <= 0 || dim <= 0) return abi::fail(SWB_ERR_ARG, "empty corpus");
+    const int vec = 16 / esize_of(x_dtype);
+    if (dim % vec)
+        return abi::fail(SWB_ERR_ARG, "the dimension must be a multiple of %d for %s rows (16-byte row chunks); "
+                                      "pad the vectors with zeros",
+                         vec, x_dtype == 0 ? "float32" : "float16");
+    if (reinterpret_cast<uintptr_t>(X) % 16) return abi::fail(SWB_ERR_ARG, "X must be 16-byte aligned");
+    if (team != 4 && team != 8 && team != 16 && team != 32)
+        return abi::fail(SWB_ERR_TEAM, "team_size must be 4, 8, 16 or 32");
+    if (L < 1 || L > MAXL) return abi::fail(SWB_ERR_ARG, "L exceeds MAXL (%d)", MAXL);
+    return SWB_OK;
+}
+
+bool pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
+
+template <typename KernelT>
+int launch(KernelT kern, dim3 grid, int threads, size_t smem, cudaStream_t st, const Knobs& K) {
+    if ((long long)smem > abi::max_smem_optin())
+        return abi::fail(SWB_ERR_SMEM, "the search needs %zu B of shared memory per block; the device allows %d. "
+                                       "Lower L or the dimension.",
+                         smem, abi::max_smem_optin());
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute");
+    }
+    kern<<<grid, threads, smem, st>>>(K);
+    return abi::cuda_check("search kernel launch");
+}
+
+#define SWB_DISPATCH(KERNEL, TEAMV, DT, ...)                                                   \
+    [&]() -> int {                                                                             \
+        if ((DT) == SWB_F32) {                                                                 \
+            switch (TEAMV) {                                                                   \
+                case 4: return launch(KERNEL<4, float>, __VA_ARGS__);                          \
+                case 8: return launch(KERNEL<8, float>, __VA_ARGS__);                          \
+                case 16: return launch(KERNEL<16, float>, __VA_ARGS__);                        \
+                default: return launch(KERNEL<32, float>, __VA_ARGS__);                        \
+            }                                                                                  \
+        }                                                                                      \
+        switch (TEAMV) {                                                                       \
+            case 4: return launch(KERNEL<4, __half>, __VA_ARGS__);                             \
+            case 8: return launch(KERNEL<8, __half>, __VA_ARGS__);                             \
+            case 16: return launch(KERNEL<16, __half>, __VA_ARGS__);                           \
+            default: return launch(KERNEL<32, __half>, __VA_ARGS__);                           \
+        }                                                                                      \
+    }()
+
+void fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int team, int L, bool q_shared) {
+    std::memset(&K, 0, sizeof(K));
+    K.X = X;
+    K.n = n;
+    K.dim = dim;
+    K.rowbytes = dim * esize_of(x_dtype);
+    K.L = L;
+    K.R = pick_ring(K.rowbytes, team);
+    K.q_shared = q_shared ? 1 : 0;
+    const Layout lay = warp_layout(L, K.R, K.rowbytes, q_shared ? 0 : dim * 4);
+    K.warp_bytes = lay.total;
+}
+
+}  // namespace
+
+extern "C" int swb_search_init(const void* X, int x_dtype, int64_t n, int dim, const float* Qv,
+                               const int32_t* seeds, int Q, int J, int V, int32_t* ids, float* dist,
+                               uint8_t* expanded, uint8_t* lineage, int L, int32_t* visited, int H,
+                               int32_t* counters, int metric, int team, uint64_t* cache, int Hc, float* bound,
+                               void* stream) {
+    int rc = common_checks(X, x_dtype, n, dim, team, L);
+    if (rc) return rc;
+    if (Q <= 0 || J <= 0) return SWB_OK;
+    if (Q > SWB_MAX_BATCH)
+        return abi::fail(SWB_ERR_BATCH, "batch of %d queries exceeds the 65535 one call allows; split the batch", Q);
+    if (V < 1 || V > MAXV) return abi::fail(SWB_ERR_ARG, "seeds per branch must be 1..%d", MAXV);
+    if (!pow2(H)) return abi::fail(SWB_ERR_ARG, "visited table size must be a power of two");
+    if (Hc > 0 && !pow2(Hc)) return abi::fail(SWB_ERR_ARG, "cache size must be a power of two");
+    if (!Qv || !seeds || !ids || !dist || !expanded || !lineage || !counters || (H > 1 && !visited))
+        return abi::fail(SWB_ERR_ARG, "null state buffer");
+    Knobs K;
+    fill_common(K, X, x_dtype, n, dim, team, L, false);
+    K.Qv = Qv; K.seeds = seeds; K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
+    K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
+    K.metric = metric; K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound;
+    K.W = 4;
+    const long long warps = (long long)Q * J;
+    dim3 grid((unsigned)((warps + K.W - 1) / K.W));
+    const size_t smem = (size_t)K.W * K.warp_bytes;
+    return SWB_DISPATCH(init_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+}
+
+extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim, const int32_t* G, int D,
+                                  const float* Qv, int32_t* ids, float* dist, uint8_t* expanded, uint8_t* lineage,
+                                  int Q, int J, int L, int32_t* visited, int H, int32_t* counters, int metric,
+                                  int team, int delta, int max_expansions, int policy, int V, float stop_eps,
+                                  int kstop, uint64_t* cache, int Hc, float* bound, int exclusive,
+                                  int stall_patience, float crowd_frac, const int32_t* active, int n_active,
+                                  int32_t* status, void* stream) {
+    int rc = common_checks(X, x_dtype, n, dim, team, L);
+    if (rc) return rc;
+    if (!G || D < 1 || D > MAXD) return abi::fail(SWB_ERR_ARG, "graph degree must be 1..%d", MAXD);
+    if (V > 256) return abi::fail(SWB_ERR_ARG, "lineage count exceeds 256 (lineage is a uint8)");
+    if (!pow2(H)) return abi::fail(SWB_ERR_ARG, "visited table size must be a power of two");
+    if (Hc > 0 && !pow2(Hc)) return abi::fail(SWB_ERR_ARG, "cache size must be a power of two");
+    if (Q <= 0 || J <= 0 || delta <= 0) return SWB_OK;
+    if (active && n_active <= 0) return SWB_OK;
+    Knobs K;
+    fill_common(K, X, x_dtype, n, dim, team, L, false);
+    K.G = G; K.D = D; K.Qv = Qv; K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
+    K.Q = Q; K.J = J; K.V = V < 1 ? 1 : V; K.visited = visited; K.H = H; K.counters = counters;
+    K.metric = metric; K.delta = delta; K.max_exp = max_expansions; K.policy = policy;
+    K.stop_eps = stop_eps; K.kstop = kstop;
+    K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound; K.exclusive = exclusive && Hc > 0;
+    K.stall_patience = stall_patience; K.crowd_frac = crowd_frac;
+    K.active = active; K.n_active = active ? n_active : 0; K.status = status;
+    K.W = 4;
+    const long long warps = active ? (long long)n_active : (long long)Q * J;
+    dim3 grid((unsigned)((warps + K.W - 1) / K.W));
+    const size_t smem = (size_t)K.W * K.warp_bytes;
+    return SWB_DISPATCH(advance_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+}
+
+extern "C" int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int32_t* qdone, void* stream) {
+    if (Q <= 0) return SWB_OK;
+    if (Hc > 0 && !cache) return abi::fail(SWB_ERR_ARG, "cache is null");
+    const int64_t words = (Hc > 0) ? (int64_t)Q * Hc : 0;
+    const int64_t work = words / 2 > Q ? words / 2 : Q;
+    int blocks = (int)((work + 255) / 256);
+    const int cap = abi::num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    prepare_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(Q, Hc > 0 ? cache : nullptr, words, bound, qdone);
+    return abi::cuda_check("prepare kernel launch");
+}
+
+extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, const int32_t* G, int D,
+                                const float* Qv, const int32_t* seeds, int Q, int J, int V, int k, int L, int B,
+                                int metric, int team, int policy, float stop_eps, int kstop, int32_t* visited,
+                                int H, uint64_t* cache, int Hc, float* bound, int exclusive, int stall_patience,
+                                float crowd_frac, int32_t* branch_ids, float* branch_dist, int32_t* qdone,
+                                int32_t* out_ids, float* out_dist, int32_t* ids, float* dist, uint8_t* expanded,
+                                uint8_t* lineage, int32_t* counters, int32_t* status, void* stream) {
+    int rc = common_checks(X, x_dtype, n, dim, team, L);
+    if (rc) return rc;
+    if (!G || D < 1 || D > MAXD) return abi::fail(SWB_ERR_ARG, "graph degree must be 1..%d", MAXD);
+    if (Q > SWB_MAX_BATCH)
+        return abi::fail(SWB_ERR_BATCH, "batch of %d queries exceeds the 65535 one call allows; split the batch", Q);
+    if (V < 1 || V > MAXV) return abi::fail(SWB_ERR_ARG, "seeds per branch must be 1..%d", MAXV);
+    if (!pow2(H)) return abi::fail(SWB_ERR_ARG, "visited table size must be a power of two");
+    if (Hc > 0 && !pow2(Hc)) return abi::fail(SWB_ERR_ARG, "cache size must be a power of two");
+    if (k < 1) return abi::fail(SWB_ERR_ARG, "k must be positive");
+    if (!branch_ids || !branch_dist || !qdone || !out_ids || !out_dist || !seeds || !Qv)
+        return abi::fail(SWB_ERR_ARG, "null buffer");
+    if (Q <= 0 || J <= 0) return SWB_OK;
+    if ((ids || dist || expanded || lineage) && !(ids && dist && expanded && lineage))
+        return abi::fail(SWB_ERR_ARG, "state outputs must be all given or all null");
+    Knobs K;
+    fill_common(K, X, x_dtype, n, dim, team, L, true);
+    K.G = G; K.D = D; K.Qv = Qv; K.seeds = seeds;
+    K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
+    K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
+    K.metric = metric; K.max_exp = B; K.delta = B; K.policy = policy; K.stop_eps = stop_eps; K.kstop = kstop;
+    K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound; K.exclusive = exclusive && Hc > 0;
+    K.stall_patience = stall_patience; K.crowd_frac = crowd_frac;
+    K.status = status; K.k = k; K.kk = k < L ? k : L;
+    K.branch_ids = branch_ids; K.branch_dist = branch_dist; K.qdone = qdone;
+    K.out_ids = out_ids; K.out_dist = out_dist;
+    if (J > 4 * MAXD) return abi::fail(SWB_ERR_ARG, "at most %d branches per query", 4 * MAXD);
+    int W = abi::env_int("SWB_WARPS", 4);
+    if (W > J) W = J;
+    if (W < 1) W = 1;
+    if (W > 8) W = 8;
+    K.W = W;
+    dim3 grid((unsigned)((J + W - 1) / W), (unsigned)Q);
+    const size_t smem = (size_t)align16(dim * 4) + (size_t)W * K.warp_bytes;
+    return SWB_DISPATCH(fused_kernel, team, x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
+}
+
+extern "C" int swb_merge_branches(const int32_t* bids, const float* bdist, int Q, int J, int kk, int k,
+                                  int32_t* out_ids, float* out_dist, void* stream) {
+    if (Q <= 0) return SWB_OK;
+    const int n = J * kk;
+    if (k < 1 || k > n) return abi::fail(SWB_ERR_ARG, "k must be in 1..J*kk");
+    int padded = 1;
+    while (padded < n) padded <<= 1;
+    const size_t smem = (size_t)padded * 8;
+    if ((long long)smem > abi::max_smem_optin())
+        return abi::fail(SWB_ERR_SMEM, "merge needs %zu B of shared memory for %d candidates", smem, n);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute");
+    }
+    merge_kernel<<<Q, 256, smem, (cudaStream_t)stream>>>(bids, bdist, n, k, padded, out_ids, out_dist);
+    return abi::cuda_check("merge kernel launch");
+}

@@ -1,0 +1,195 @@
+"""The public interface: build an index over vectors, then search it.
+
+Drop-in for swann/index.py (geniussyn/SWANN):
+
+    import swann_b200 as swann
+    index = swann.Index.build(X, metric="ip")      # X: (n, d) float32 / float16
+    ids, dist = index.search(Q, k=10)
+
+Same constructor, `build`, `search(queries, k, config, **overrides)`, `save`,
+`load`, `SearchConfig` defaults and errors.  One addition: `devices=[...]`
+replicates the corpus, graph and catalogue on several GPUs and splits each
+query batch across them in contiguous shards -- queries are independent, so
+the shards need no communication and the results are concatenated in order.
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import _engine as E
+from . import _lib as N
+from . import _select as S
+
+METRICS = {"ip": E.METRIC_IP, "l2": E.METRIC_L2}
+MAX_BATCH = 65535
+
+
+@dataclass
+class SearchConfig:
+    """Knobs, with the reference's defaults (swann/index.py:26-45).
+
+    branches  trajectories one query is split into (warps of the GPU).
+    queue     width of each branch's candidate queue.
+    budget    cap on expansions per branch; `stop_eps` usually binds first.
+    stop_eps  stop a branch once its best candidate is worse than the query's
+              current k-th answer by this fraction; negative disables it.
+    team      lanes cooperating on one distance (fixes the summation order).
+    """
+    branches: int = 32
+    queue: int = 12
+    budget: int = 64
+    stop_eps: float = 0.05
+    team: int = 16
+    k: int = 10
+
+
+class _Replica:
+    """What one GPU holds: the corpus, the graph, the catalogue and its rows."""
+
+    def __init__(self, X, G, catalogue, dev):
+        self.dev = dev
+        self.X = X if X.device == dev else X.to(dev)
+        self.G = G if G.device == dev else G.to(dev)
+        self.catalogue = catalogue if catalogue.device == dev else catalogue.to(dev)
+        self.cat_rows = S.pool_vectors(self.X.float(), self.catalogue)
+
+
+class Index:
+    """A proximity graph plus the vectors it indexes, resident on one or more GPUs."""
+
+    def __init__(self, vectors: torch.Tensor, graph: torch.Tensor, metric: str = "ip",
+                 catalogue: torch.Tensor | None = None, catalogue_size: int = 4096, seed: int = 0,
+                 devices=None):
+        if vectors.device.type != "cuda":
+            raise ValueError("vectors must already be on the GPU")
+        if vectors.dtype not in (torch.float32, torch.float16):
+            raise ValueError("vectors must be float32 or float16")
+        if metric not in METRICS:
+            raise ValueError(f"metric must be one of {sorted(METRICS)}")
+        vec = 8 if vectors.dtype == torch.float16 else 4
+        if vectors.shape[1] % vec:
+            raise ValueError(f"the dimension must be a multiple of {vec} for {vectors.dtype} vectors "
+                             "(the kernels read 16-byte row chunks); pad the vectors with zeros")
+        self.X = vectors.contiguous()
+        self.G = graph.to(device=self.X.device, dtype=torch.int32).contiguous()
+        self.metric = metric
+        self._m = METRICS[metric]
+        if catalogue is None:
+            n = self.X.shape[0]
+            rng = np.random.default_rng(seed)
+            pick = np.sort(rng.permutation(n)[:min(catalogue_size, n)])
+            catalogue = torch.from_numpy(pick.astype(np.int64)).to(self.X.device)
+        self.catalogue = catalogue.to(self.X.device)
+        if devices is None:
+            devs = [self.X.device]
+        else:
+            devs = [torch.device("cuda", d) if isinstance(d, int) else torch.device(d) for d in devices]
+        self._replicas = [_Replica(self.X, self.G, self.catalogue, d) for d in devs]
+        self._cat = self._replicas[0].cat_rows
+
+    @property
+    def devices(self):
+        return [r.dev for r in self._replicas]
+
+    # -- construction ----------------------------------------------------
+    @classmethod
+    def build(cls, vectors, metric: str = "ip", degree: int = 96, candidates: int = 128,
+              alpha: float = 1.2, **kw) -> "Index":
+        """Build a graph over `vectors` on the GPU (exact sweep, prune, reverse)."""
+        from .build import build_graph
+        X = _as_cuda(vectors)
+        G = build_graph(X, metric=metric, degree=degree, candidates=candidates, alpha=alpha)
+        return cls(X, G, metric=metric, **kw)
+
+    # -- search ----------------------------------------------------------
+    def search(self, queries, k: int = 10, config: SearchConfig | None = None, **overrides):
+        """Return (ids, distances), each (nq, k), as numpy arrays."""
+        ids, dist = self.search_tensors(queries, k=k, config=config, **overrides)
+        return ids.cpu().numpy(), dist.cpu().numpy()
+
+    def search_tensors(self, queries, k: int = 10, config: SearchConfig | None = None, **overrides):
+        """Like `search`, but returns torch tensors on the first device."""
+        cfg = config or SearchConfig(k=k)
+        for key, value in overrides.items():
+            if not hasattr(cfg, key):
+                raise TypeError(f"unknown search option {key!r}")
+            setattr(cfg, key, value)
+        nq = int(queries.shape[0])
+        if nq > MAX_BATCH:
+            raise ValueError(f"batch of {nq} exceeds the 65535 the kernel's grid allows; split it")
+        reps = self._replicas
+        bounds = np.linspace(0, nq, len(reps) + 1).astype(np.int64)
+        host = queries if not isinstance(queries, torch.Tensor) or queries.device.type == "cpu" else None
+        if host is not None and isinstance(host, np.ndarray):
+            host = torch.from_numpy(np.ascontiguousarray(host))
+        outs = []
+        for r, (a, b) in zip(reps, zip(bounds[:-1], bounds[1:])):
+            if b <= a:
+                continue
+            with torch.cuda.device(r.dev):
+                if host is not None:
+                    Qd = host[a:b].to(r.dev, non_blocking=True)
+                else:
+                    Qd = queries[a:b].to(r.dev, non_blocking=True)
+                Qd = Qd.float().contiguous()
+                ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
+                seeds = r.catalogue[ent].to(torch.int32)
+                ids, dist, ctr, status = _search_device(r, Qd, seeds, k, cfg, self._m)
+                outs.append((ids, dist, ctr, status))
+        if E._OVERFLOW_GUARD:
+            for _, _, ctr, status in outs:
+                if ctr is not None and int(ctr[..., 2].sum()) != 0:
+                    raise RuntimeError("visited table overflowed: raise the budget used for sizing")
+                if int(status[0]) != 0:
+                    raise N.SwannError(int(status[0]), "a device-side wait timed out during the search")
+        dev0 = reps[0].dev
+        ids = torch.cat([o[0].to(dev0) for o in outs]) if outs else torch.empty((0, k), dtype=torch.int32)
+        dist = torch.cat([o[1].to(dev0) for o in outs]) if outs else torch.empty((0, k))
+        return ids, dist
+
+    # -- persistence -----------------------------------------------------
+    def save(self, path) -> None:
+        """Write graph.npy, catalogue.npy and index.json (the reference's format)."""
+        path = Path(path)
+        path.mkdir(parents=True, exist_ok=True)
+        np.save(path / "graph.npy", self.G.cpu().numpy())
+        np.save(path / "catalogue.npy", self.catalogue.cpu().numpy())
+        (path / "index.json").write_text(json.dumps(
+            {"metric": self.metric, "n": int(self.X.shape[0]), "d": int(self.X.shape[1]),
+             "degree": int(self.G.shape[1])}, indent=2))
+
+    @classmethod
+    def load(cls, path, vectors, **kw) -> "Index":
+        path = Path(path)
+        meta = json.loads((path / "index.json").read_text())
+        X = _as_cuda(vectors)
+        G = torch.from_numpy(np.load(path / "graph.npy")).to(X.device)
+        cat = torch.from_numpy(np.load(path / "catalogue.npy")).to(X.device)
+        return cls(X, G, metric=meta["metric"], catalogue=cat, **kw)
+
+    def __repr__(self) -> str:
+        n, d = self.X.shape
+        return (f"Index(n={n:,}, d={d}, degree={self.G.shape[1]}, metric={self.metric!r}, "
+                f"dtype={self.X.dtype}, devices={len(self._replicas)})")
+
+
+def _search_device(r: _Replica, Qd, seeds, k, cfg, metric):
+    """The fused search on one replica: shared table, bound and claims on,
+    per-branch visited tables elided (swann/index.py:105-109)."""
+    ids, dist, ctr, status = E.search_fused_lean(
+        r.X, r.G, Qd, seeds, k=k, L=cfg.queue, B=cfg.budget, metric=metric, team_size=cfg.team,
+        stop_eps=cfg.stop_eps, shared_cache=True, shared_bound=True, exclusive=True, elide_visited=True)
+    return ids, dist, ctr, status
+
+
+def _as_cuda(a) -> torch.Tensor:
+    if isinstance(a, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(a))
+    if a.device.type != "cuda":
+        a = a.cuda()
+    return a.contiguous()

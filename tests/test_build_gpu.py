@@ -1,0 +1,121 @@
+"""GPU parity of the graph build (swann_b200/build.py over csrc/build.cu).
+
+  * candidates: every position of every list equals the exact (double) answer
+    or is a tie within fp32 noise of it;
+  * prune and reverse: bit-exact against the oracle given the same inputs
+    (same candidates / same graph), which is the north-star gate;
+  * the whole build end to end against the oracle's CPU build.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import oracle as O
+from swann_b200 import build as B
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+GOLD = cases.__file__.rsplit("/", 1)[0]
+
+
+def _exact(X, i, js, metric):
+    a = X[i].astype(np.float64)
+    V = X[js].astype(np.float64)
+    return 1.0 - V @ a if metric == 0 else ((V - a) ** 2).sum(1)
+
+
+def _tol(X, metric):
+    d = X.shape[1]
+    scale = 1.0 if metric == 0 else 2.0 * float((X.astype(np.float64) ** 2).sum(1).max())
+    return 4.0 * d * 2.0 ** -24 * scale
+
+
+def _check_candidates(X, got, want, metric):
+    tol = _tol(X, metric)
+    bad = []
+    for i in range(X.shape[0]):
+        if np.array_equal(got[i], want[i]):
+            continue
+        if np.any(np.abs(_exact(X, i, got[i], metric) - _exact(X, i, want[i], metric)) > tol):
+            bad.append(i)
+    return bad
+
+
+@pytest.mark.parametrize("metric,dtype,C", [(0, np.float32, 64), (1, np.float32, 128), (0, np.float16, 128),
+                                            (1, np.float32, 33)])
+def test_candidates_exact_except_ties(metric, dtype, C):
+    X = cases.build_corpus(3000, 64, seed=5 + metric, metric=metric).astype(dtype)
+    Xg = torch.from_numpy(X).to(DEV)
+    idx, dst = B.knn_candidates(Xg, C, chunk=1024, metric="ip" if metric == 0 else "l2", col_chunk=1000)
+    Xf = X.astype(np.float32)
+    want, wd = O.knn_candidates(Xf, C, metric)
+    got = idx.cpu().numpy()
+    assert not _check_candidates(Xf, got, want, metric)
+    # distances are the exact ones up to fp32 evaluation noise
+    assert np.abs(dst.cpu().numpy() - wd).max() <= _tol(Xf, metric) * 4
+    # ascending, self excluded
+    d = dst.cpu().numpy()
+    assert (np.diff(d, axis=1) >= 0).all()
+    assert not (got == np.arange(X.shape[0])[:, None]).any()
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_prune_bitexact_given_candidates(metric):
+    """Same candidates in, same graph out, bit for bit (oracle's arithmetic)."""
+    name = "ip" if metric == 0 else "l2"
+    g = np.load(f"{GOLD}/build.npz")
+    X = cases.build_corpus(1000, 64, seed=11 + metric, metric=metric)
+    cand, cd = g[f"{name}_cand"], g[f"{name}_cdist"]
+    Xg = torch.from_numpy(X).to(DEV)
+    got = B.robust_prune(Xg, torch.from_numpy(cand).to(DEV), torch.from_numpy(cd).to(DEV), 32, alpha=1.2,
+                         metric=name).cpu().numpy()
+    want = O.robust_prune(X, cand, cd, 32, 1.2, metric)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_reverse_bitexact_given_graph(metric):
+    name = "ip" if metric == 0 else "l2"
+    g = np.load(f"{GOLD}/build.npz")
+    X = cases.build_corpus(1000, 64, seed=11 + metric, metric=metric)
+    G1 = g[f"{name}_prune"]
+    Xg = torch.from_numpy(X).to(DEV)
+    got = B.add_reverse(Xg, torch.from_numpy(G1).to(DEV), 32, alpha=1.2, metric=name).cpu().numpy()
+    want = O.add_reverse(X, G1, 32, 1.2, 64, metric)
+    assert np.array_equal(got, want)
+
+
+def test_prune_wide_candidates_and_sinks():
+    """C = 128 candidates, degree 64, with -1 holes and an all-empty row."""
+    rng = np.random.default_rng(4)
+    X = cases.build_corpus(600, 40, seed=2, metric=1)
+    cand, cd = O.knn_candidates(X, 128, 1)
+    cand[5, 60:] = -1
+    cand[7, :] = -1
+    Xg = torch.from_numpy(X).to(DEV)
+    got = B.robust_prune(Xg, torch.from_numpy(cand).to(DEV), torch.from_numpy(cd).to(DEV), 64, alpha=1.2,
+                         metric="l2").cpu().numpy()
+    want = O.robust_prune(X, cand, cd, 64, 1.2, 1)
+    assert np.array_equal(got, want)
+    assert (got[7] == -1).all()
+    del rng
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_build_graph_end_to_end(metric):
+    """The GPU build of a 2000-row corpus against the oracle's build: the
+    candidates agree except ties, and the final graph is identical wherever
+    the candidates were."""
+    name = "ip" if metric == 0 else "l2"
+    X = cases.build_corpus(2000, 64, seed=21 + metric, metric=metric)
+    Xg = torch.from_numpy(X).to(DEV)
+    idx, dst = B.knn_candidates(Xg, 64, metric=name)
+    want, _ = O.knn_candidates(X, 64, metric)
+    assert not _check_candidates(X, idx.cpu().numpy(), want, metric)
+    G = B.build_graph(Xg, metric=name, degree=32, candidates=64).cpu().numpy()
+    # the oracle's prune + reverse from the GPU's own candidates: bit-exact
+    c, d = idx.cpu().numpy(), dst.cpu().numpy()
+    G1 = O.robust_prune(X, c, d, 32, 1.2, metric)
+    G2 = O.add_reverse(X, G1, 32, 1.2, 64, metric)
+    assert np.array_equal(G, G2)
