@@ -1,0 +1,594 @@
+#!/usr/bin/env python
+"""SWANN on B200: QPS at recall@10 >= 0.95, HBM roofline, build seconds.
+
+Workload (the north star's headline): n = 1,000,000 rows,
+d = 1536, drawn from 1,000 anisotropic Gaussian clusters (per-dimension scales
+log-uniform in [0.1, 1]), rows L2-normalised and stored fp16; fp32 queries
+normalised from the same mixture; inner product; k = 10; a batch of 65,535
+queries per GPU per step; degree-64 graph (candidates 128, alpha 1.2) built by
+this package's kernels.  Seeded synthetic data stands in for the corpora the
+reference measured on.
+
+A step is one Index.search of the batch.  The operating point (branches,
+queue, stop_eps) is the fastest one whose recall@10 against exact fp32 ground
+truth is >= 0.95, chosen before timing on a fixed subset of the batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: (n, d, clusters, dtype, metric, batch)
+    "c3": dict(n=1_000_000, d=1536, clusters=1000, half=True, metric="ip", batch=65535, k=10,
+               desc="C3: 1M x 1536 fp16 inner-product corpus, 1000 anisotropic clusters"),
+    "c2": dict(n=1_000_000, d=960, clusters=100, half=False, metric="l2", batch=10000, k=10,
+               desc="C2: 1M x 960 fp32 L2 corpus, 100-component isotropic mixture (sigma 0.3)"),
+    "c1": dict(n=10_000, d=128, clusters=0, half=False, metric="l2", batch=100, k=10,
+               desc="C1: 10k x 128 fp32 N(0,1) L2 corpus (CPU-runnable case)"),
+    "small": dict(n=100_000, d=256, clusters=100, half=True, metric="ip", batch=8192, k=10,
+                  desc="small: 100k x 256 fp16 inner-product corpus (smoke-scale)"),
+}
+LADDER = [(32, 12), (32, 16), (64, 16), (64, 24), (128, 32)]
+EPS = [0.0, 0.02, 0.05, 0.08, 0.12, 0.2, 0.3]
+TARGET = 0.95
+
+
+# ---------------------------------------------------------------------------
+# synthetic data (seeded, generated on the device in chunks)
+
+def gen_mixture(n, d, clusters, seed, dev, half, normalise, aniso=True, chunk=1 << 16, sigma=0.3):
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)   # the mixture itself is shared by corpus and queries
+    if clusters:
+        centres = torch.randn((clusters, d), generator=g, device=dev)
+        if aniso:
+            lo, hi = np.log(0.1), np.log(1.0)
+            scales = torch.exp(lo + (hi - lo) * torch.rand((clusters, d), generator=g, device=dev))
+        else:
+            scales = torch.full((clusters, d), sigma, device=dev)
+    gs = torch.Generator(device=dev)
+    gs.manual_seed(seed)
+    out = torch.empty((n, d), dtype=torch.float16 if half else torch.float32, device=dev)
+    for a in range(0, n, chunk):
+        b = min(n, a + chunk)
+        z = torch.randn((b - a, d), generator=gs, device=dev)
+        if clusters:
+            c = torch.randint(0, clusters, (b - a,), generator=gs, device=dev)
+            x = centres[c] + scales[c] * z
+        else:
+            x = z
+        if normalise:
+            x = x / x.norm(dim=1, keepdim=True)
+        out[a:b] = x.to(out.dtype)
+    return out
+
+
+def make_corpus(cfg, dev):
+    aniso = cfg["metric"] == "ip"
+    norm = cfg["metric"] == "ip"
+    X = gen_mixture(cfg["n"], cfg["d"], cfg["clusters"], 1, dev, cfg["half"], norm, aniso=aniso)
+    return X
+
+
+def make_queries(cfg, dev, rank, batch):
+    aniso = cfg["metric"] == "ip"
+    norm = cfg["metric"] == "ip"
+    return gen_mixture(batch, cfg["d"], cfg["clusters"], 1000 + rank, dev, False, norm, aniso=aniso)
+
+
+@torch.no_grad()
+def exact_topk(X, Q, k, metric, rows=1024):
+    """Exact fp32 ground truth (fp32 GEMM, no TF32)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    Xf = X.float()
+    xn = (Xf * Xf).sum(1) if metric == "l2" else None
+    out = []
+    for a in range(0, Q.shape[0], rows):
+        s = Q[a:a + rows] @ Xf.T
+        if metric == "ip":
+            out.append(torch.topk(s, k, dim=1).indices)
+        else:
+            out.append(torch.topk(xn.view(1, -1) - 2.0 * s, k, dim=1, largest=False).indices)
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del Xf
+    return torch.cat(out).cpu().numpy()
+
+
+def recall(ids, truth, k):
+    ids = np.asarray(ids)[:, :k]
+    hit = [len(set(a.tolist()) & set(b.tolist())) for a, b in zip(ids, truth[:, :k])]
+    return float(np.mean(hit)) / k
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("SWB_CLOCK_LOG", f"/tmp/swb_clocks_{os.getpid()}.csv"))
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+        return False
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                rows.append((float(p[1]), float(p[2]), p[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i in range(4) if r[i].lower().startswith("active")})
+        load = [s for s, _, _ in rows]
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(m for _, m, _ in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+
+def measured_peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of the top kernel from a committed ncu summary."""
+    p = ROOT / "profiles" / f"{name}.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_index(cfg, dev, world, rank):
+    """The graph by this package's kernels: single GPU, or row blocks over
+    the ranks with NCCL all-gathers (swann_b200.dist.build_sharded)."""
+    from swann_b200 import build as B
+    from swann_b200 import dist as D
+    t = {}
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    n = cfg["n"]
+    if world == 1:
+        X = make_corpus(cfg, dev)
+        torch.cuda.synchronize()
+        t["generate_s"] = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"])
+        torch.cuda.synchronize()
+        t["sweep_s"] = time.perf_counter() - t1
+        t1 = time.perf_counter()
+        G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"])
+        torch.cuda.synchronize()
+        t["prune_s"] = time.perf_counter() - t1
+        del cand, cd
+        t1 = time.perf_counter()
+        G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"])
+        torch.cuda.synchronize()
+        t["reverse_s"] = time.perf_counter() - t1
+    else:
+        Xfull = make_corpus(cfg, dev)   # each rank keeps only its row block as its "input"
+        a, b = D.shard_bounds(n, world)[rank]
+        Xl = Xfull[a:b].contiguous()
+        del Xfull
+        torch.cuda.synchronize()
+        t["generate_s"] = time.perf_counter() - t0
+        stage = {}
+
+        def sweep(Xa, r0, r1):
+            s = time.perf_counter()
+            c, d = B.knn_candidates(Xa, 128, metric=cfg["metric"], rows=(r0, r1))
+            torch.cuda.synchronize()
+            stage["sweep_s"] = time.perf_counter() - s
+            return c, d
+
+        def prune(Xa, c, d):
+            s = time.perf_counter()
+            g = B.robust_prune(Xa, c, d, 64, alpha=1.2, metric=cfg["metric"])
+            torch.cuda.synchronize()
+            stage["prune_s"] = time.perf_counter() - s
+            return g
+
+        def reverse(Xa, G1, r0, r1):
+            s = time.perf_counter()
+            g = B.add_reverse(Xa, G1, 64, alpha=1.2, metric=cfg["metric"], rows=(r0, r1))
+            torch.cuda.synchronize()
+            stage["reverse_s"] = time.perf_counter() - s
+            return g
+
+        X, G = D.build_sharded(Xl, n, sweep, prune, reverse)
+        t.update(stage)
+    torch.cuda.synchronize()
+    t["total_s"] = time.perf_counter() - t0
+    return X, G, t
+
+
+def cpu_baseline(X, G, Q, seeds, cfg, op, budget_s=15.0):
+    """The reference's CPU search path (swann/_refcpu.py, restated in C by the
+    oracle) on the host cores: independent branches, merged; timed on a
+    bounded sample of the batch."""
+    from oracle import oracle as O
+    Xh = X.float().cpu().numpy() if X.dtype == torch.float16 else X.cpu().numpy()
+    Gh = G.cpu().numpy()
+    Qh = Q.cpu().numpy()
+    Sh = seeds.cpu().numpy()
+    cores = O.cpu_count()
+    vec = 8 if X.dtype == torch.float16 else 4
+    metric = 0 if cfg["metric"] == "ip" else 1
+    kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=metric, team=16, vec=vec, stop_eps=op["stop_eps"],
+              kstop=min(cfg["k"], op["queue"]), threads=cores)
+    m = cores * 2
+    t = time.perf_counter()
+    O.search(Xh, Gh, Qh[:m], Sh[:m], **kw)
+    el = time.perf_counter() - t
+    m2 = int(min(Qh.shape[0], max(m, m * budget_s / max(el, 1e-3))))
+    t = time.perf_counter()
+    O.search(Xh, Gh, Qh[:m2], Sh[:m2], **kw)
+    el = time.perf_counter() - t
+    return {"value": m2 / el, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{m2} queries of the timed batch, the reference's CPU search (independent branches, "
+                      f"_refcpu semantics) at the chosen branches/queue/stop_eps, C oracle on {cores} threads",
+            "seconds": el}
+
+
+def calibrate(index, Qs, truth, cfg):
+    """Fastest (branches, queue, stop_eps) with recall >= TARGET on Qs."""
+    best = None
+    tried = []
+    for branches, queue in LADDER:
+        found = False
+        for eps in EPS:
+            ids, _ = index.search_tensors(Qs, k=cfg["k"], branches=branches, queue=queue, stop_eps=eps)
+            torch.cuda.synchronize()
+            r = recall(ids.cpu().numpy(), truth, cfg["k"])
+            if r < TARGET:
+                tried.append((branches, queue, eps, r, None))
+                continue
+            ts = []
+            for _ in range(2):
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                index.search_tensors(Qs, k=cfg["k"], branches=branches, queue=queue, stop_eps=eps)
+                s1.record()
+                torch.cuda.synchronize()
+                ts.append(s0.elapsed_time(s1))
+            tried.append((branches, queue, eps, r, min(ts)))
+            if best is None or min(ts) < best[4]:
+                best = (branches, queue, eps, r, min(ts))
+            found = True
+            break   # larger eps only costs more at this (branches, queue)
+        if found and best is not None and branches >= 64:
+            break
+    return best, tried
+
+
+def run(args):
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["batch"] = args.batch
+    import swann_b200 as swann
+    from swann_b200 import _engine as E
+    from swann_b200 import _select as S
+
+    X, G, build_t = build_index(cfg, dev, world, rank)
+    index = swann.Index(X, G, metric=cfg["metric"])
+    batch = cfg["batch"]
+    Q = make_queries(cfg, dev, rank, batch)
+    gt_n = min(batch, args.gt)
+    truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
+
+    # operating point: chosen on rank 0, shared
+    if rank == 0:
+        best, tried = calibrate(index, Q[:gt_n], truth, cfg)
+        if best is None:
+            best = max(tried, key=lambda t: t[3])
+        op = dict(branches=best[0], queue=best[1], stop_eps=best[2])
+    else:
+        op, tried = None, []
+    if world > 1:
+        import torch.distributed as dist
+        box = [op]
+        dist.broadcast_object_list(box, src=0)
+        op = box[0]
+
+    # Size the per-query distance table from what the queries actually claim:
+    # four times the busiest query's claims (load <= 25%), a power of two.
+    ent = S.select_nearest(Q[:gt_n], index._cat, op["branches"], metric=index._m)
+    sd = index.catalogue[ent].to(torch.int32)
+    _, _, ctr, _ = E.search_fused_lean(X, G, Q[:gt_n], sd, k=cfg["k"], L=op["queue"], B=64, metric=index._m,
+                                       team_size=16, stop_eps=op["stop_eps"], shared_cache=True,
+                                       shared_bound=True, exclusive=2, elide_visited=True)
+    claims = (ctr[..., 5].to(torch.int64).sum(1) + op["branches"]).max().item()
+    ref_slots = E.cache_size(op["branches"], 64, G.shape[1])
+    slots = min(ref_slots, max(4096, E.next_pow2(4 * int(claims))))
+    index.table_slots = slots
+    table = {"slots": slots, "reference_slots": ref_slots, "max_claims_per_query": int(claims),
+             "max_load": round(claims / slots, 4)}
+
+    def step():
+        return index.search_tensors(Q, k=cfg["k"], **op)
+
+    # recall of the full-batch operating point, on the ground-truth subset
+    ids, _ = step()
+    torch.cuda.synchronize()
+    rec = recall(ids[:gt_n].cpu().numpy(), truth, cfg["k"])
+
+    # -- device-resident timing (value) ----------------------------------
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    clocks = clk.summary()
+    value = world * batch * args.steps / (ms / 1e3)
+
+    # -- end to end through the public API with host buffers -------------
+    Qh = Q.cpu().pin_memory()
+    for _ in range(max(1, args.warmup // 2)):
+        index.search(Qh, k=cfg["k"], **op)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out_ids, out_d = index.search(Qh, k=cfg["k"], **op)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = {"value": world * batch * args.steps / e2e_s, "unit": "queries/s",
+           "h2d_bytes_per_step": int(Qh.numel() * Qh.element_size()),
+           "d2h_bytes_per_step": int(out_ids.nbytes + out_d.nbytes)}
+
+    # -- roofline of the dominant kernel (the fused search) ----------------
+    ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
+    seeds = index.catalogue[ent].to(torch.int32)
+    kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=index._m, team_size=16, stop_eps=op["stop_eps"],
+              shared_cache=True, shared_bound=True, exclusive=2, elide_visited=True, table_slots=slots)
+    _, _, ctr, _ = E.search_fused_lean(X, G, Q, seeds, **kw)
+    torch.cuda.synchronize()
+    c = ctr.to(torch.int64)
+    nodes = int(c[..., 5].sum()) + int(batch * op["branches"])      # claimed + seeds
+    exps = int(c[..., 0].sum())
+    esize = X.element_size()
+    alg_bytes = nodes * cfg["d"] * esize + exps * G.shape[1] * 4
+    lib = E.N.lib()
+    kt = []
+    for _ in range(max(3, args.steps)):
+        # prepare + fused, each bracketed by events on the launching stream
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        Jq = op["branches"]
+        Hc = slots
+        cache = E._WS.get("cache", batch * Hc, torch.int64, dev).view(batch, -1)
+        bound = E._WS.get("bound", batch, torch.float32, dev)
+        qdone = E._WS.get("qdone", batch, torch.int32, dev)
+        kk = min(cfg["k"], op["queue"])
+        bi = E._WS.get("branch_ids", batch * Jq * kk, torch.int32, dev)
+        bd = E._WS.get("branch_dist", batch * Jq * kk, torch.float32, dev)
+        oi = torch.empty((batch, cfg["k"]), dtype=torch.int32, device=dev)
+        od = torch.empty((batch, cfg["k"]), dtype=torch.float32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        s = stream.cuda_stream
+        ev[0].record(stream)
+        E.N.check(lib.swb_search_prepare(batch, E.N.ptr(cache), Hc, E.N.ptr(bound), E.N.ptr(qdone), s))
+        ev[1].record(stream)
+        rc = lib.swb_search_fused(
+            E.N.ptr(X), E.N.dtype_code(X), X.shape[0], X.shape[1], E.N.ptr(G), G.shape[1], E.N.ptr(Q),
+            E.N.ptr(seeds), batch, Jq, 1, cfg["k"], op["queue"], 64, index._m, 16, 0, float(op["stop_eps"]),
+            cfg["k"], None, 1, E.N.ptr(cache), Hc, E.N.ptr(bound), 2, 0, 0.0, E.N.ptr(bi), E.N.ptr(bd),
+            E.N.ptr(qdone), E.N.ptr(oi), E.N.ptr(od), None, None, None, None, None, E.N.ptr(status), s)
+        E.N.check(rc)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        kt.append((ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])))
+    prep_ms = statistics.median(t[0] for t in kt)
+    fused_ms = statistics.median(t[1] for t in kt)
+    peak, peak_kind = measured_peak_hbm()
+    achieved = alg_bytes / (fused_ms / 1e3) / 1e9
+    prof = profile_traffic(f"search_fused_{args.config}")
+    roofline = {"bound": "hbm", "kernel": "swb::fused_kernel", "achieved": round(achieved, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": prof.get("traffic_per_launch") if prof else None,
+                "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": round(fused_ms, 3),
+                "prepare_ms": round(prep_ms, 3),
+                "per_query": {"distinct_nodes_scored": nodes / batch, "expansions": exps / batch}}
+
+    line = {
+        "metric": f"QPS at recall@10>={TARGET} ({cfg['desc']}, batch {batch} per GPU)",
+        "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
+        "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], "storage": "f16" if cfg["half"] else "f32",
+                   "metric": cfg["metric"], "batch_per_gpu": batch, "k": cfg["k"], **op, "budget": 64, "team": 16,
+                   "recall@10": round(rec, 4), "recall_sample": gt_n, "graph": "degree 64, candidates 128, alpha 1.2",
+                   "claims": "strict (exclusive=2)", "table": table,
+                   "l2": "inputs larger than L2 (corpus %.1f GB; rows gathered at random)" % (
+                       X.numel() * X.element_size() / 1e9),
+                   "parallelism": f"query shards x{world}, replicas"},
+        "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": 2 * args.steps,
+        "build": {k: round(v, 3) for k, v in build_t.items()},
+        "calibration": [{"branches": b, "queue": q, "stop_eps": e, "recall": round(r, 4),
+                         "ms": None if t is None else round(t, 3)} for b, q, e, r, t in tried],
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(X, G, Q, seeds, cfg, op)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference's own CPU search path (the C restatement of
+    swann/_refcpu.py, independent branches merged) on the host cores, on the
+    same workload; the index is built on the GPU by this package first
+    (setup, untimed: the reference's CPU build would take days at this size)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["batch"] = args.batch
+    import swann_b200 as swann
+    from oracle import oracle as O
+    X, G, _ = build_index(cfg, dev, 1, 0)
+    index = swann.Index(X, G, metric=cfg["metric"])
+    Q = make_queries(cfg, dev, 0, cfg["batch"])
+    op = dict(branches=32, queue=12, stop_eps=0.05)
+    from swann_b200 import _select as S
+    ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
+    seeds = index.catalogue[ent].to(torch.int32)
+    Xh = X.float().cpu().numpy()
+    Gh, Qh, Sh = G.cpu().numpy(), Q.cpu().numpy(), seeds.cpu().numpy()
+    cores = O.cpu_count()
+    metric = 0 if cfg["metric"] == "ip" else 1
+    kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=metric, team=16, vec=8 if cfg["half"] else 4,
+              stop_eps=op["stop_eps"], kstop=min(cfg["k"], op["queue"]), threads=cores)
+    per = cores * 2
+    times = []
+    for i in range(args.warmup + args.steps):
+        a = (i * per) % max(1, Qh.shape[0] - per)
+        t = time.perf_counter()
+        O.search(Xh, Gh, Qh[a:a + per], Sh[a:a + per], **kw)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t)
+    el = sum(times)
+    value = per * args.steps / el
+    line = {"metric": f"QPS at recall@10>={TARGET} ({cfg['desc']}, batch {cfg['batch']} per GPU)",
+            "value": round(value, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+            "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
+            "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], **op, "budget": 64, "team": 16},
+            "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": cores, "kind": "port",
+                             "sample": f"{per} queries per step (C restatement of swann/_refcpu.py, independent "
+                                       f"branches, {cores} threads); index built on the GPU beforehand"},
+            "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="swann_b200", choices=["swann_b200", "reference"])
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
+    ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--gt", type=int, default=8192)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -82,7 +82,9 @@ class SearchState:
     cache: torch.Tensor = None
     # Per-query k-th-best bound [Q]; empty = off.
     bound: torch.Tensor = None
-    exclusive: bool = False
+    # 1: skip nodes another branch has scored (the reference's rule); 2: also
+    # skip nodes another branch has claimed but not yet scored; 0: off
+    exclusive: int = 0
     # int32 [1] device status word: a device wait that gave up writes
     # SWB_ERR_TIMEOUT here
     status: torch.Tensor = None
@@ -208,7 +210,7 @@ def _alloc_state(X, Q, J, L, V, B, D, metric, team_size, policy, stop_eps, kstop
         st.cache = torch.empty((Q, cache_size(J, B, D)), dtype=torch.int64, device=dev)
     else:
         st.cache = _empty(torch.int64, dev, (0, 0))
-    st.exclusive = bool(exclusive and shared_cache and J > 1)
+    st.exclusive = int(exclusive) if (shared_cache and J > 1) else 0
     st.bound = (torch.empty((Q,), dtype=torch.float32, device=dev) if (shared_bound and J > 1)
                 else _empty(torch.float32, dev))
     st.status = torch.zeros((1,), dtype=torch.int32, device=dev)
@@ -366,7 +368,7 @@ _WS = Workspace()
 
 
 def _fused(X, G, Qv, seeds, k, L, B, metric, team_size, policy, stop_eps, shared_cache, shared_bound,
-           exclusive, stall_patience, crowd_frac, elide_visited, kstop, keep_state):
+           exclusive, stall_patience, crowd_frac, elide_visited, kstop, keep_state, table_slots=None):
     _check_inputs(X, Qv)
     if not (G.is_cuda and G.dtype == torch.int32 and G.is_contiguous()):
         raise ValueError("G: contiguous cuda int32")
@@ -385,12 +387,13 @@ def _fused(X, G, Qv, seeds, k, L, B, metric, team_size, policy, stop_eps, shared
     else:
         st = None
         visited = _WS.get("visited", Q * J * H, torch.int32, dev) if H > 1 else _empty(torch.int32, dev)
-        cache = (_WS.get("cache", Q * cache_size(J, B, D), torch.int64, dev).view(Q, -1)
+        Hc = table_slots or cache_size(J, B, D)
+        cache = (_WS.get("cache", Q * Hc, torch.int64, dev).view(Q, -1)
                  if (shared_cache and J > 1) else _empty(torch.int64, dev, (0, 0)))
         bound = _WS.get("bound", Q, torch.float32, dev) if (shared_bound and J > 1) else _empty(torch.float32, dev)
         status = torch.zeros((1,), dtype=torch.int32, device=dev)
         ctr = torch.empty((Q, J, NCTR), dtype=torch.int32, device=dev)
-    excl = bool(exclusive and shared_cache and J > 1)
+    excl = int(exclusive) if (shared_cache and J > 1) else 0
     Hc = cache.shape[1] if cache.numel() else 0
     bi = _WS.get("branch_ids", Q * J * kk, torch.int32, dev)
     bd = _WS.get("branch_dist", Q * J * kk, torch.float32, dev)
@@ -426,12 +429,13 @@ def search_fused(X, G, Qv, seeds, k=10, L=16, B=16, metric=METRIC_IP, team_size=
 
 def search_fused_lean(X, G, Qv, seeds, k=10, L=16, B=16, metric=METRIC_IP, team_size=32, policy=POLICY_BEST,
                       stop_eps=-1.0, shared_cache=False, shared_bound=False, exclusive=False, stall_patience=0,
-                      crowd_frac=0.0, elide_visited=False, kstop=None):
+                      crowd_frac=0.0, elide_visited=False, kstop=None, table_slots=None):
     """The fused search writing only results, counters [Q, J, NCTR] and the
-    status word (the path Index.search runs).  Returns (ids, dist, ctr, status)."""
+    status word (the path Index.search runs).  `table_slots` overrides the
+    per-query table size (a power of two).  Returns (ids, dist, ctr, status)."""
     oi, od, _, ctr, status = _fused(X, G, Qv, seeds, k, L, B, metric, team_size, policy, stop_eps, shared_cache,
                                     shared_bound, exclusive, stall_patience, crowd_frac, elide_visited, kstop,
-                                    False)
+                                    False, table_slots)
     return oi, od, ctr, status
 
 

@@ -69,9 +69,10 @@ def _dots(A, B, exact_half):
 
 
 @torch.no_grad()
-def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact=None):
+def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact=None, rows=None):
     """Exact top-C neighbours by the corpus's metric, self excluded
-    (swann/build.py:30-43).  Returns (idx int32 [n, C], dst f32 [n, C])."""
+    (swann/build.py:30-43).  Returns (idx int32 [m, C], dst f32 [m, C]) for
+    rows=(r0, r1) (default: every row), m = r1 - r0."""
     m = _m(metric)
     if not Xg.is_cuda:
         raise ValueError("vectors must be on the GPU")
@@ -82,18 +83,19 @@ def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact
         half_exact = bool(Xg.dtype == torch.float16 or (small and torch.equal(Xg, Xg.half().float())))
     Xf = Xg.float().contiguous()
     norms = row_norms(Xf) if m == METRIC_L2 else None
-    idx = torch.empty((n, C), dtype=torch.int32, device=Xg.device)
-    dst = torch.empty((n, C), dtype=torch.float32, device=Xg.device)
+    R0, R1 = (0, n) if rows is None else rows
+    idx = torch.empty((R1 - R0, C), dtype=torch.int32, device=Xg.device)
+    dst = torch.empty((R1 - R0, C), dtype=torch.float32, device=Xg.device)
     lib = N.lib()
     with torch.cuda.device(Xg.device):
         s = N.stream_of(Xg)
-        for r0 in range(0, n, chunk):
-            r1 = min(r0 + chunk, n)
+        for r0 in range(R0, R1, chunk):
+            r1 = min(r0 + chunk, R1)
             for c0 in range(0, n, col_chunk):
                 c1 = min(c0 + col_chunk, n)
                 D = _dots(Xf[r0:r1], Xf[c0:c1], half_exact).contiguous()
                 rc = lib.swb_topc_block(N.ptr(D), r1 - r0, D.shape[1], c1 - c0, r0, c0, N.ptr(norms), m, C,
-                                        N.ptr(idx[r0:r1]), N.ptr(dst[r0:r1]), int(c0 > 0), s)
+                                        N.ptr(idx[r0 - R0:r1 - R0]), N.ptr(dst[r0 - R0:r1 - R0]), int(c0 > 0), s)
                 N.check(rc, "knn_candidates")
                 del D
     return idx, dst

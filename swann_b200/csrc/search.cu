@@ -537,7 +537,11 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
                     int cslot = -1, claimed = 0;
                     float d = FLT_MAX;
                     if (ctab) d = cache_probe(ctab, K.Hc, v, cslot, claimed);
-                    const bool taken = K.exclusive && cslot >= 0 && !claimed && d != FLT_MAX;
+                    // exclusive == 1: a node another branch has scored is off limits
+                    // (local_search.cu:553); exclusive == 2 also treats a claim whose
+                    // distance is still being computed as off limits
+                    const bool taken = K.exclusive && cslot >= 0 && !claimed &&
+                                       (d != FLT_MAX || K.exclusive == 2);
                     if (taken) {
                         ++hits;
                         ++cov;
@@ -1034,7 +1038,8 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     K.Q = Q; K.J = J; K.V = V < 1 ? 1 : V; K.visited = visited; K.H = H; K.counters = counters;
     K.metric = metric; K.delta = delta; K.max_exp = max_expansions; K.policy = policy;
     K.stop_eps = stop_eps; K.kstop = kstop;
-    K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound; K.exclusive = exclusive && Hc > 0;
+    K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound;
+    K.exclusive = Hc > 0 ? exclusive : 0;
     K.stall_patience = stall_patience; K.crowd_frac = crowd_frac;
     K.active = active; K.n_active = active ? n_active : 0; K.status = status;
     K.W = 4;
@@ -1084,7 +1089,8 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
     K.metric = metric; K.max_exp = B; K.delta = B; K.policy = policy; K.stop_eps = stop_eps; K.kstop = kstop;
-    K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound; K.exclusive = exclusive && Hc > 0;
+    K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound;
+    K.exclusive = Hc > 0 ? exclusive : 0;
     K.stall_patience = stall_patience; K.crowd_frac = crowd_frac;
     K.status = status; K.k = k; K.kk = k < L ? k : L;
     K.branch_ids = branch_ids; K.branch_dist = branch_dist; K.qdone = qdone;
