@@ -45,6 +45,10 @@ CONFIGS = {
                desc="C1: 10k x 128 fp32 N(0,1) L2 corpus (CPU-runnable case)"),
     "small": dict(n=100_000, d=256, clusters=100, half=True, metric="ip", batch=8192, k=10,
                   desc="small: 100k x 256 fp16 inner-product corpus (smoke-scale)"),
+    # C3-shaped profiling case: same row width and mixture model, a corpus
+    # (0.6 GB) still larger than L2, small enough for an ncu capture
+    "c3s": dict(n=200_000, d=1536, clusters=200, half=True, metric="ip", batch=4096, k=10,
+                desc="C3-shaped profiling case: 200k x 1536 fp16 inner product, 200 clusters"),
 }
 LADDER = [(32, 12), (32, 16), (64, 16), (64, 24), (128, 32)]
 EPS = [0.0, 0.02, 0.05, 0.08, 0.12, 0.2, 0.3]
@@ -360,21 +364,25 @@ def run(args):
     from swann_b200 import _select as S
 
     X, G, build_t = build_index(cfg, dev, world, rank)
+    torch.cuda.empty_cache()
     index = swann.Index(X, G, metric=cfg["metric"])
     batch = cfg["batch"]
     Q = make_queries(cfg, dev, rank, batch)
     gt_n = min(batch, args.gt)
     truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
 
-    # operating point: chosen on rank 0, shared
-    if rank == 0:
+    # operating point: chosen on rank 0, shared (or fixed on the command line)
+    if args.fixed:
+        b, q, e = args.fixed.split(",")
+        op, tried = dict(branches=int(b), queue=int(q), stop_eps=float(e)), []
+    elif rank == 0:
         best, tried = calibrate(index, Q[:gt_n], truth, cfg)
         if best is None:
             best = max(tried, key=lambda t: t[3])
         op = dict(branches=best[0], queue=best[1], stop_eps=best[2])
     else:
         op, tried = None, []
-    if world > 1:
+    if world > 1 and not args.fixed:
         import torch.distributed as dist
         box = [op]
         dist.broadcast_object_list(box, src=0)
@@ -581,6 +589,7 @@ def main():
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--gt", type=int, default=8192)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--fixed", default="", help="branches,queue,stop_eps: skip the calibration")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
