@@ -143,6 +143,26 @@ SWB_API int swb_topc_block(const float* dots, int64_t rows, int64_t ld, int64_t 
                    int64_t col0, const float* norms, int metric, int C, int32_t* idx, float* dst,
                    int resume, void* stream);
 
+/* Replaces knn_candidates (swann/build.py:30-43) whole: for rows
+ * [row0, row0 + rows) of X, the C nearest rows of X by the metric, ascending by
+ * (distance, id), the row itself carrying 3.4e38 -- X x X^T on tcgen05 (TMEM
+ * accumulators, TMA-fed) with the per-row top-C selection in the epilogue.
+ *   SWB_F16 rows: X fp16 [n, dim], dim % 64 == 0, X_lo = NULL (exact products)
+ *   SWB_F32 rows: X = tf32 high parts, X_lo = low parts (swb_split_tf32),
+ *                 dim % 32 == 0 (3xTF32: hi*hi + hi*lo + lo*hi)
+ *   norms [n] float32 squared row norms (l2 only)
+ *   idx/dst [rows, C] int32 / float32 (out), C <= 256
+ *   workspace: at least swb_sweep_workspace() bytes
+ *   status: optional int32 device word, SWB_ERR_TIMEOUT if a wait ran out */
+SWB_API int swb_sweep_topc(const void* X, const void* X_lo, int x_dtype, int64_t n, int dim,
+                   const float* norms, int64_t row0, int64_t rows, int C, int metric,
+                   int32_t* idx, float* dst, void* workspace, uint64_t ws_bytes,
+                   int32_t* status, void* stream);
+SWB_API uint64_t swb_sweep_workspace(int64_t n, int64_t rows, int C, int x_dtype);
+
+/* fp32 -> (hi, lo): hi = x rounded to tf32 precision, lo = x - hi (exact). */
+SWB_API int swb_split_tf32(const float* X, int64_t count, float* hi, float* lo, void* stream);
+
 /* Squared norms of the rows of X in sequential-fmaf order (the build's l2 norms). */
 SWB_API int swb_row_norms(const void* X, int x_dtype, int64_t n, int dim, float* norms, void* stream);
 

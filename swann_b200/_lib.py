@@ -39,6 +39,10 @@ SIGNATURES = {
                                 _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "swb_topc_block": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _vp, _i32, _vp]),
     "swb_row_norms": (_i32, [_vp, _i32, _i64, _i32, _vp, _vp]),
+    "swb_sweep_topc": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _u64,
+                              _vp, _vp]),
+    "swb_sweep_workspace": (_u64, [_i64, _i64, _i32, _i32]),
+    "swb_split_tf32": (_i32, [_vp, _i64, _vp, _vp, _vp]),
     "swb_prune": (_i32, [_vp, _i64, _i32, _vp, _vp, _i64, _i32, _i32, _f32, _i32, _vp, _vp]),
     "swb_reverse": (_i32, [_vp, _i64, _i32, _vp, _i32, _f32, _i32, _i32, _i64, _i64, _vp, _vp, _u64, _vp]),
     "swb_reverse_workspace": (_u64, [_i64, _i64, _i32, _i32]),

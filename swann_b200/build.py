@@ -17,6 +17,8 @@ with fmaf, so their output is reproducible bit for bit from the same input.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib as N
@@ -68,11 +70,30 @@ def _dots(A, B, exact_half):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def _pad_cols(X, mult):
+    d = X.shape[1]
+    if d % mult == 0:
+        return X
+    P = torch.zeros((X.shape[0], d + (-d) % mult), dtype=X.dtype, device=X.device)
+    P[:, :d] = X
+    return P
+
+
 @torch.no_grad()
-def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact=None, rows=None):
+def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact=None, rows=None,
+                   method=None, row_block=1 << 18):
     """Exact top-C neighbours by the corpus's metric, self excluded
     (swann/build.py:30-43).  Returns (idx int32 [m, C], dst f32 [m, C]) for
-    rows=(r0, r1) (default: every row), m = r1 - r0."""
+    rows=(r0, r1) (default: every row), m = r1 - r0.
+
+    method="mma" (default): swb_sweep_topc, the tcgen05 sweep with the top-C
+    fused (fp16-valued rows exactly in kind::f16, others in 3xTF32).
+    method="gemm": a library GEMM per row chunk and swb_topc_block.
+    The default is "mma" unless SWB_SWEEP names the other."""
+    if method is None:
+        method = os.environ.get("SWB_SWEEP", "mma")
+    if method == "mma":
+        return _knn_mma(Xg, C, metric, half_exact, rows, row_block)
     m = _m(metric)
     if not Xg.is_cuda:
         raise ValueError("vectors must be on the GPU")
@@ -98,6 +119,47 @@ def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact
                                         N.ptr(idx[r0 - R0:r1 - R0]), N.ptr(dst[r0 - R0:r1 - R0]), int(c0 > 0), s)
                 N.check(rc, "knn_candidates")
                 del D
+    return idx, dst
+
+
+def _knn_mma(Xg, C, metric, half_exact, rows, row_block):
+    m = _m(metric)
+    if not Xg.is_cuda:
+        raise ValueError("vectors must be on the GPU")
+    n = Xg.shape[0]
+    if half_exact is None:
+        small = n * Xg.shape[1] <= (1 << 26)
+        half_exact = bool(Xg.dtype == torch.float16 or (small and torch.equal(Xg.float(), Xg.half().float())))
+    norms = row_norms(Xg.float().contiguous()) if m == METRIC_L2 else None
+    if half_exact:
+        lo = None
+        hi = _pad_cols(Xg.half().contiguous(), 64)
+        code = N.F16
+    else:
+        Xf = _pad_cols(Xg.float().contiguous(), 32)
+        hi = torch.empty_like(Xf)
+        lo = torch.empty_like(Xf)
+    R0, R1 = (0, n) if rows is None else rows
+    idx = torch.empty((R1 - R0, C), dtype=torch.int32, device=Xg.device)
+    dst = torch.empty((R1 - R0, C), dtype=torch.float32, device=Xg.device)
+    status = torch.zeros(1, dtype=torch.int32, device=Xg.device)
+    lib = N.lib()
+    with torch.cuda.device(Xg.device):
+        s = N.stream_of(Xg)
+        if not half_exact:
+            N.check(lib.swb_split_tf32(N.ptr(Xf), Xf.numel(), N.ptr(hi), N.ptr(lo), s), "split")
+            del Xf
+            code = N.F32
+        for r0 in range(R0, R1, row_block):
+            r1 = min(R1, r0 + row_block)
+            ws_bytes = int(lib.swb_sweep_workspace(n, r1 - r0, C, code))
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=Xg.device)
+            rc = lib.swb_sweep_topc(N.ptr(hi), N.ptr(lo), code, n, hi.shape[1], N.ptr(norms), r0, r1 - r0, C, m,
+                                    N.ptr(idx[r0 - R0:r1 - R0]), N.ptr(dst[r0 - R0:r1 - R0]), N.ptr(ws), ws_bytes,
+                                    N.ptr(status), s)
+            N.check(rc, "knn_candidates")
+    if int(status[0]) != 0:
+        raise N.SwannError(int(status[0]), "a device-side wait timed out in the sweep")
     return idx, dst
 
 

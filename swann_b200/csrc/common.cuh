@@ -174,4 +174,69 @@ __device__ __forceinline__ float team_reduce(float acc) {
     return acc;
 }
 
+// The same TEAM-lane distance on TP physical lanes (TP divides TEAM).  Physical
+// lane p carries the S = TEAM / TP logical lanes p, p + TP, ..., each with its
+// own accumulator, so one lane runs S independent add chains instead of one.
+// Every logical lane still sums its own chunks in the reference's order, and
+// the tree is unchanged: its levels with offsets >= TP pair logical lanes that
+// share a physical lane (p + j*TP with p + (j + off/TP)*TP) and are done here
+// as local adds of exactly the same operands; split_reduce does the rest with
+// shuffles.  Returns logical lane p's value after the local levels.
+template <int TEAM, int TP, typename XT>
+__device__ __forceinline__ float split_partial(const float* __restrict__ sq, const XT* __restrict__ row, int dim,
+                                               int metric, int p) {
+    constexpr int V = VecN<XT>::N;
+    constexpr int S = TEAM / TP;
+    const int nch = dim / V;
+    float acc[S];
+#pragma unroll
+    for (int j = 0; j < S; ++j) acc[j] = 0.f;
+    if (metric == METRIC_IP) {
+        for (int c0 = 0; c0 < nch; c0 += TEAM) {
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+                const int c = c0 + p + j * TP;
+                if (c < nch) {
+                    float x[V], q[V];
+                    widen16(row + c * V, x);
+#pragma unroll
+                    for (int i = 0; i < V; i += 4) widen16(sq + c * V + i, q + i);
+#pragma unroll
+                    for (int i = 0; i < V; ++i) acc[j] = __fadd_rn(acc[j], __fmul_rn(q[i], x[i]));
+                }
+            }
+        }
+    } else {
+        for (int c0 = 0; c0 < nch; c0 += TEAM) {
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+                const int c = c0 + p + j * TP;
+                if (c < nch) {
+                    float x[V], q[V];
+                    widen16(row + c * V, x);
+#pragma unroll
+                    for (int i = 0; i < V; i += 4) widen16(sq + c * V + i, q + i);
+#pragma unroll
+                    for (int i = 0; i < V; ++i) {
+                        const float df = __fsub_rn(q[i], x[i]);
+                        acc[j] = __fadd_rn(acc[j], __fmul_rn(df, df));
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int h = S / 2; h > 0; h >>= 1)
+#pragma unroll
+        for (int j = 0; j < h; ++j) acc[j] = __fadd_rn(acc[j], acc[j + h]);
+    return acc[0];
+}
+
+template <int TP>
+__device__ __forceinline__ float split_reduce(float acc) {
+#pragma unroll
+    for (int off = TP / 2; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(FULL, acc, off, TP));
+    return acc;
+}
+
 }  // namespace swb

@@ -65,7 +65,7 @@ struct Knobs {
     int32_t* qdone;
     int32_t* out_ids;
     float* out_dist;
-    int W, R, warp_bytes, q_shared;
+    int W, R, warp_bytes, q_shared, cmax;
 };
 
 __host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
@@ -75,8 +75,9 @@ struct Layout {
         retired, total;
 };
 
-// q_bytes = 0 when the query lives once per CTA rather than per warp
-__host__ __device__ inline Layout warp_layout(int L, int R, int rowbytes, int q_bytes) {
+// q_bytes = 0 when the query lives once per CTA rather than per warp; cmax
+// (a power of two >= 32) bounds the candidates, seeds and rows of one step
+__host__ __device__ inline Layout warp_layout(int L, int R, int rowbytes, int q_bytes, int cmax) {
     Layout w;
     int o = 0;
     w.ring = o; o += R * rowbytes;      // 16-byte multiples: first, so rows stay aligned
@@ -90,13 +91,13 @@ __host__ __device__ inline Layout warp_layout(int L, int R, int rowbytes, int q_
     w.s_l = o; o += align16(L);
     w.n_e = o; o += align16(L);
     w.n_l = o; o += align16(L);
-    w.c_id = o; o += MAXD * 4;
-    w.c_d = o; o += MAXD * 4;
-    w.c_l = o; o += MAXD;
-    w.w_v = o; o += MAXD * 4;
-    w.w_slot = o; o += MAXD * 4;
-    w.w_d = o; o += MAXD * 4;
-    w.w_aux = o; o += MAXD * 4;
+    w.c_id = o; o += cmax * 4;
+    w.c_d = o; o += cmax * 4;
+    w.c_l = o; o += align16(cmax);
+    w.w_v = o; o += cmax * 4;         // w_v .. w_aux are contiguous (4 * cmax ints)
+    w.w_slot = o; o += cmax * 4;
+    w.w_d = o; o += cmax * 4;
+    w.w_aux = o; o += cmax * 4;
     w.retired = o; o += 32;
     w.total = align16(o);
     return w;
@@ -216,34 +217,35 @@ __device__ __forceinline__ void issue_row(const Knobs& K, const WarpMem& w, int 
     bulk_g2s(w.ring + (size_t)s * K.rowbytes, src, (uint32_t)K.rowbytes, &w.mbar[s]);
 }
 
-// Scores the m rows listed in w.w_v with TEAM-lane teams, 32/TEAM rows at a
-// time, while later rows stream into the ring.  Rows with w.w_slot >= 0 are
-// published to the per-query table `ctab` as soon as they are scored.
-// Returns false (after draining the copies in flight) if a wait ran out.
-template <int TEAM, typename XT>
+// Scores the m rows listed in w.w_v, 32/TP rows at a time (each row on TP
+// lanes carrying one TEAM-lane team, common.cuh), while later rows stream into
+// the ring.  Rows with w.w_slot >= 0 are published to the per-query table
+// `ctab` as soon as they are scored.  Returns false (after draining the copies
+// in flight) if a wait ran out.
+template <int TEAM, int TP, typename XT>
 __device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, const float* sq,
                            uint64_t* ctab, int lane) {
     if (m == 0) return true;
-    constexpr int P = 32 / TEAM;
-    const int R = K.R;
-    const int team = lane / TEAM, tl = lane % TEAM;
+    constexpr int RPR = 32 / TP;   // rows per round
+    const int R = K.R;             // >= RPR
+    const int grp = lane / TP, p = lane % TP;
     const int first = m < R ? m : R;
     if (lane < first) issue_row<XT>(K, w, lane);
     // Items [base, min(m, base + R)) are in flight at the top of each round,
     // one per slot.
-    for (int base = 0; base < m; base += P) {
-        const int i = base + team;
+    for (int base = 0; base < m; base += RPR) {
+        const int i = base + grp;
         float acc = 0.f;
         bool good = true;
         if (i < m) {
             const int s = i % R;
             good = mbar_wait(&w.mbar[s], (ring.phases >> s) & 1u);
             if (good)
-                acc = team_partial<TEAM, XT>(sq, reinterpret_cast<const XT*>(w.ring + (size_t)s * K.rowbytes),
-                                             K.dim, K.metric, tl);
+                acc = split_partial<TEAM, TP, XT>(
+                    sq, reinterpret_cast<const XT*>(w.ring + (size_t)s * K.rowbytes), K.dim, K.metric, p);
         }
-        acc = team_reduce<TEAM>(acc);
-        if (tl == 0 && i < m && good) {
+        acc = split_reduce<TP>(acc);
+        if (p == 0 && i < m && good) {
             const float d = (K.metric == METRIC_IP) ? __fsub_rn(1.f, acc) : acc;
             w.w_d[i] = d;
             const int slot = w.w_slot[i];
@@ -252,9 +254,9 @@ __device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, 
         // a slot's parity advances only when its wait succeeded
         const unsigned goodmask = __ballot_sync(FULL, good);
 #pragma unroll
-        for (int t = 0; t < P; ++t) {
+        for (int t = 0; t < RPR; ++t) {
             const int ii = base + t;
-            if (ii < m && ((goodmask >> (t * TEAM)) & 1u)) ring.phases ^= 1u << (ii % R);
+            if (ii < m && ((goodmask >> (t * TP)) & 1u)) ring.phases ^= 1u << (ii % R);
         }
         if (goodmask != FULL) {
             // A wait ran out.  Record it, then wait (bounded) for every copy
@@ -262,7 +264,7 @@ __device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, 
             const int end = min(m, base + R);
             for (int ii = base; ii < end; ++ii) {
                 const int t = ii - base;
-                if (t < P && ((goodmask >> (t * TEAM)) & 1u)) continue;
+                if (t < RPR && ((goodmask >> (t * TP)) & 1u)) continue;
                 const int s = ii % R;
                 if (lane == 0) mbar_wait(&w.mbar[s], (ring.phases >> s) & 1u);
                 ring.phases ^= 1u << s;
@@ -272,7 +274,7 @@ __device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, 
             return false;
         }
         __syncwarp();
-        if (lane < P) {
+        if (lane < RPR) {
             const int ni = base + lane + R;
             if (ni < m) issue_row<XT>(K, w, ni);
         }
@@ -413,7 +415,7 @@ __device__ __forceinline__ void swap_queue(WarpMem& w) {
 
 // Seeds -> sorted queue (local_search.cu:318-350).  Duplicate seeds keep their
 // first occurrence (the CPU reference's rule, _refcpu.py:68-74).
-template <int TEAM, typename XT>
+template <int TEAM, int TP, typename XT>
 __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring,
                             int* ctr) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
@@ -455,7 +457,7 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
     }
     for (int off = 16; off > 0; off >>= 1) fails += __shfl_xor_sync(FULL, fails, off);
     __syncwarp();
-    score_rows<TEAM, XT>(K, w, m, ring, sq, nullptr, lane);
+    score_rows<TEAM, TP, XT>(K, w, m, ring, sq, nullptr, lane);
     ctr[1] += m;
     ctr[2] += fails;
     for (int t = lane; t < m; t += 32) {
@@ -477,7 +479,7 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
 }
 
 // The walk: up to `delta` expansions (local_search.cu:451-683).
-template <int TEAM, typename XT>
+template <int TEAM, int TP, typename XT>
 __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring, int* ctr,
                      int delta) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
@@ -570,7 +572,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             claimed_rows += __popc(__ballot_sync(FULL, nst[t] == 2 && nsl[t] >= 0));
         }
         __syncwarp();
-        if (!score_rows<TEAM, XT>(K, w, m, ring, sq, ctab, lane)) break;
+        if (!score_rows<TEAM, TP, XT>(K, w, m, ring, sq, ctab, lane)) break;
 #pragma unroll
         for (int t = 0; t < 4; ++t)
             if (nst[t] == 2) {
@@ -709,14 +711,14 @@ __device__ void store_state(const Knobs& K, const WarpMem& w, size_t bid, int la
 // ---------------------------------------------------------------------------
 // kernels
 
-template <int TEAM, typename XT>
+template <int TEAM, int TP, typename XT>
 __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = blockIdx.x * K.W + warp;
     if (g >= K.Q * K.J) return;
     const int q = g / K.J, j = g % K.J;
-    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4);
+    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4, K.cmax);
     WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
     Ring ring;
     ring_setup(K, w, lane, ring);
@@ -732,11 +734,11 @@ __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs
     if (K.bound && j == 0 && lane == 0) K.bound[q] = FLT_MAX;
     __syncwarp();
     int ctr[NCTR];
-    init_branch<TEAM, XT>(K, w, q, j, lane, w.q, ring, ctr);
+    init_branch<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr);
     store_state(K, w, (size_t)q * K.J + j, lane, ctr);
 }
 
-template <int TEAM, typename XT>
+template <int TEAM, int TP, typename XT>
 __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -750,14 +752,14 @@ __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Kn
         flat = g;
     }
     const int q = flat / K.J, j = flat % K.J;
-    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4);
+    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4, K.cmax);
     WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
     Ring ring;
     ring_setup(K, w, lane, ring);
     load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
     int ctr[NCTR];
     load_state(K, w, (size_t)flat, lane, ctr);
-    walk<TEAM, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
+    walk<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
     __syncwarp();
     store_state(K, w, (size_t)flat, lane, ctr);
 }
@@ -803,7 +805,7 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
     for (int t = w + lane; t < k; t += 32) { oi[t] = -1; od[t] = __int_as_float(0x7f800000); }
 }
 
-template <int TEAM, typename XT>
+template <int TEAM, int TP, typename XT>
 __global__ void __launch_bounds__(256) fused_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -814,13 +816,13 @@ __global__ void __launch_bounds__(256) fused_kernel(const __grid_constant__ Knob
     load_query(sq, K.Qv + (size_t)q * K.dim, K.dim, threadIdx.x, blockDim.x);
     __syncthreads();
     if (j >= K.J) return;
-    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, 0);
+    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, 0, K.cmax);
     WarpMem w = carve(smem + qbytes + (size_t)warp * K.warp_bytes, lay);
     Ring ring;
     ring_setup(K, w, lane, ring);
     int ctr[NCTR];
-    init_branch<TEAM, XT>(K, w, q, j, lane, sq, ring, ctr);
-    walk<TEAM, XT>(K, w, q, j, lane, sq, ring, ctr, K.max_exp);
+    init_branch<TEAM, TP, XT>(K, w, q, j, lane, sq, ring, ctr);
+    walk<TEAM, TP, XT>(K, w, q, j, lane, sq, ring, ctr, K.max_exp);
     __syncwarp();
     const size_t bid = (size_t)q * K.J + j;
     store_state(K, w, bid, lane, ctr);
@@ -835,7 +837,7 @@ __global__ void __launch_bounds__(256) fused_kernel(const __grid_constant__ Knob
     last = __shfl_sync(FULL, last, 0);
     if (!last) return;
     __threadfence();
-    // the walk is over: w_v .. w_aux (4 * MAXD ints, contiguous) hold the heads
+    // the walk is over: w_v .. w_aux (4 * cmax >= J ints, contiguous) hold the heads
     merge_sorted_lists(K.branch_ids + (size_t)q * K.J * K.kk, K.branch_dist + (size_t)q * K.J * K.kk, K.J, K.kk,
                        K.k, w.w_v, K.out_ids + (size_t)q * K.k, K.out_dist + (size_t)q * K.k, lane);
 }
@@ -913,16 +915,31 @@ namespace {
 
 int esize_of(int x_dtype) { return x_dtype == 0 ? 4 : 2; }
 
-int pick_ring(int rowbytes, int team) {
-    // Rows in flight per warp: a staging budget per warp, at least the rows
-    // one round scores (32 / team), at most 32 (one issuing lane each).
-    int budget = abi::env_int("SWB_RING_BYTES", 12 * 1024);
+// Physical lanes per row (common.cuh split_partial): 4 gives 8 rows per round
+// and TEAM/4 add chains per lane; 8 halves the ring a warp needs.  Wide rows
+// default to 8 so that a round's rows fit the staging budget.
+int pick_tp(int rowbytes, int team) {
+    int tp = abi::env_int("SWB_TP", 0);
+    if (tp != 4 && tp != 8) tp = (rowbytes * 8 <= abi::env_int("SWB_RING_BYTES", 12 * 1024)) ? 4 : 8;
+    if (tp > team) tp = team;
+    return tp;
+}
+
+// Rows in flight per warp: a staging budget per warp, at least one round's
+// rows (32 / tp), at most 32 (one issuing lane each).
+int pick_ring(int rowbytes, int tp) {
+    const int budget = abi::env_int("SWB_RING_BYTES", 12 * 1024);
     int r = budget / rowbytes;
-    const int p = 32 / team;
-    if (r < p) r = p;
-    if (r < 2) r = 2;
+    const int rpr = 32 / tp;
+    if (r < rpr) r = rpr;
     if (r > 32) r = 32;
     return r;
+}
+
+int pow2_at_least(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
 }
 
 int common_checks(const void* X, int x_dtype, int64_t n, int dim, int team, int L) {
@@ -957,35 +974,43 @@ int launch(KernelT kern, dim3 grid, int threads, size_t smem, cudaStream_t st, c
     return abi::cuda_check("search kernel launch");
 }
 
-#define SWB_DISPATCH(KERNEL, TEAMV, DT, ...)                                                   \
+#define SWB_CASE(KERNEL, T, P, TEAMV, TPV, DT, ...)                                           \
+    if ((TEAMV) == T && (TPV) == P)                                                            \
+        return ((DT) == SWB_F32) ? launch(KERNEL<T, P, float>, __VA_ARGS__)                    \
+                                 : launch(KERNEL<T, P, __half>, __VA_ARGS__);
+#define SWB_DISPATCH(KERNEL, TEAMV, TPV, DT, ...)                                              \
     [&]() -> int {                                                                             \
-        if ((DT) == SWB_F32) {                                                                 \
-            switch (TEAMV) {                                                                   \
-                case 4: return launch(KERNEL<4, float>, __VA_ARGS__);                          \
-                case 8: return launch(KERNEL<8, float>, __VA_ARGS__);                          \
-                case 16: return launch(KERNEL<16, float>, __VA_ARGS__);                        \
-                default: return launch(KERNEL<32, float>, __VA_ARGS__);                        \
-            }                                                                                  \
-        }                                                                                      \
-        switch (TEAMV) {                                                                       \
-            case 4: return launch(KERNEL<4, __half>, __VA_ARGS__);                             \
-            case 8: return launch(KERNEL<8, __half>, __VA_ARGS__);                             \
-            case 16: return launch(KERNEL<16, __half>, __VA_ARGS__);                           \
-            default: return launch(KERNEL<32, __half>, __VA_ARGS__);                           \
-        }                                                                                      \
+        SWB_CASE(KERNEL, 4, 4, TEAMV, TPV, DT, __VA_ARGS__)                                    \
+        SWB_CASE(KERNEL, 8, 4, TEAMV, TPV, DT, __VA_ARGS__)                                    \
+        SWB_CASE(KERNEL, 8, 8, TEAMV, TPV, DT, __VA_ARGS__)                                    \
+        SWB_CASE(KERNEL, 16, 4, TEAMV, TPV, DT, __VA_ARGS__)                                   \
+        SWB_CASE(KERNEL, 16, 8, TEAMV, TPV, DT, __VA_ARGS__)                                   \
+        SWB_CASE(KERNEL, 32, 4, TEAMV, TPV, DT, __VA_ARGS__)                                   \
+        SWB_CASE(KERNEL, 32, 8, TEAMV, TPV, DT, __VA_ARGS__)                                   \
+        return abi::fail(SWB_ERR_TEAM, "team_size must be 4, 8, 16 or 32");                   \
     }()
 
-void fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int team, int L, bool q_shared) {
+// cmax bounds what one step handles: D candidates, V seeds, and (fused) the
+// J branch heads of the final merge, which reuse 4 * cmax ints
+int fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int team, int L, bool q_shared, int D,
+                int V, int J) {
     std::memset(&K, 0, sizeof(K));
     K.X = X;
     K.n = n;
     K.dim = dim;
     K.rowbytes = dim * esize_of(x_dtype);
     K.L = L;
-    K.R = pick_ring(K.rowbytes, team);
+    const int tp = pick_tp(K.rowbytes, team);
+    K.R = pick_ring(K.rowbytes, tp);
     K.q_shared = q_shared ? 1 : 0;
-    const Layout lay = warp_layout(L, K.R, K.rowbytes, q_shared ? 0 : dim * 4);
+    int cm = pow2_at_least(D > V ? D : V);
+    const int jq = (J + 3) / 4;
+    if (cm < jq) cm = pow2_at_least(jq);
+    if (cm < 32) cm = 32;
+    K.cmax = cm;
+    const Layout lay = warp_layout(L, K.R, K.rowbytes, q_shared ? 0 : dim * 4, cm);
     K.warp_bytes = lay.total;
+    return tp;
 }
 
 }  // namespace
@@ -1006,7 +1031,7 @@ extern "C" int swb_search_init(const void* X, int x_dtype, int64_t n, int dim, c
     if (!Qv || !seeds || !ids || !dist || !expanded || !lineage || !counters || (H > 1 && !visited))
         return abi::fail(SWB_ERR_ARG, "null state buffer");
     Knobs K;
-    fill_common(K, X, x_dtype, n, dim, team, L, false);
+    const int tp = fill_common(K, X, x_dtype, n, dim, team, L, false, 1, V, 0);
     K.Qv = Qv; K.seeds = seeds; K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
     K.metric = metric; K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound;
@@ -1014,7 +1039,7 @@ extern "C" int swb_search_init(const void* X, int x_dtype, int64_t n, int dim, c
     const long long warps = (long long)Q * J;
     dim3 grid((unsigned)((warps + K.W - 1) / K.W));
     const size_t smem = (size_t)K.W * K.warp_bytes;
-    return SWB_DISPATCH(init_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH(init_kernel, team, tp, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim, const int32_t* G, int D,
@@ -1033,7 +1058,7 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     if (Q <= 0 || J <= 0 || delta <= 0) return SWB_OK;
     if (active && n_active <= 0) return SWB_OK;
     Knobs K;
-    fill_common(K, X, x_dtype, n, dim, team, L, false);
+    const int tp = fill_common(K, X, x_dtype, n, dim, team, L, false, D, 1, 0);
     K.G = G; K.D = D; K.Qv = Qv; K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V < 1 ? 1 : V; K.visited = visited; K.H = H; K.counters = counters;
     K.metric = metric; K.delta = delta; K.max_exp = max_expansions; K.policy = policy;
@@ -1046,7 +1071,7 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     const long long warps = active ? (long long)n_active : (long long)Q * J;
     dim3 grid((unsigned)((warps + K.W - 1) / K.W));
     const size_t smem = (size_t)K.W * K.warp_bytes;
-    return SWB_DISPATCH(advance_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH(advance_kernel, team, tp, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int32_t* qdone, void* stream) {
@@ -1084,7 +1109,8 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     if ((ids || dist || expanded || lineage) && !(ids && dist && expanded && lineage))
         return abi::fail(SWB_ERR_ARG, "state outputs must be all given or all null");
     Knobs K;
-    fill_common(K, X, x_dtype, n, dim, team, L, true);
+    if (J > 4 * MAXD) return abi::fail(SWB_ERR_ARG, "at most %d branches per query", 4 * MAXD);
+    const int tp = fill_common(K, X, x_dtype, n, dim, team, L, true, D, V, J);
     K.G = G; K.D = D; K.Qv = Qv; K.seeds = seeds;
     K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
@@ -1095,7 +1121,6 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.status = status; K.k = k; K.kk = k < L ? k : L;
     K.branch_ids = branch_ids; K.branch_dist = branch_dist; K.qdone = qdone;
     K.out_ids = out_ids; K.out_dist = out_dist;
-    if (J > 4 * MAXD) return abi::fail(SWB_ERR_ARG, "at most %d branches per query", 4 * MAXD);
     int W = abi::env_int("SWB_WARPS", 4);
     if (W > J) W = J;
     if (W < 1) W = 1;
@@ -1103,7 +1128,7 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.W = W;
     dim3 grid((unsigned)((J + W - 1) / W), (unsigned)Q);
     const size_t smem = (size_t)align16(dim * 4) + (size_t)W * K.warp_bytes;
-    return SWB_DISPATCH(fused_kernel, team, x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH(fused_kernel, team, tp, x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_merge_branches(const int32_t* bids, const float* bdist, int Q, int J, int kk, int k,

@@ -1,0 +1,566 @@
+// sweep_mma.cu -- the exact candidate sweep on the 5th-generation tensor cores.
+//
+// Replaces knn_candidates (swann/build.py:30-43): for a block of rows, the C
+// nearest rows of the whole corpus by the metric, with the X x X^T tiles on
+// tcgen05 and the per-row top-C selection fused into the epilogue, so the
+// n x n distance matrix never exists.
+//
+// One CTA owns 128 rows (the 128 TMEM lanes) and sweeps every column tile:
+//   warp 0      TMA producer: 128B-swizzled tiles of the row block (A) and of
+//               the column tile (B) into a ring of shared-memory stages;
+//   warp 1      MMA issuer: tcgen05.mma into one of two TMEM accumulators
+//               (BN fp32 columns each), committing each stage back to the
+//               producer and each finished tile to the epilogue;
+//   warps 2..5  epilogue: tcgen05.ld (one thread per row), distance, a filter
+//               against the row's current C-th best, a small per-row buffer
+//               in shared memory, and a merge into the row's sorted best list
+//               (global scratch) when the buffer fills.
+// The second accumulator lets the MMAs of tile t+1 run while the epilogue
+// reads tile t.
+//
+// Arithmetic.  fp16 rows (MODE_F16): kind::f16, fp16 x fp16 products are exact
+// in fp32, accumulation in fp32.  fp32 rows (MODE_TF32X3): each operand is
+// split host-side into hi = tf32(x) and lo = x - hi; the accumulator gets
+// hi*hi + hi*lo + lo*hi (kind::tf32), which carries about 2^-22 relative error
+// per product, the fp32-faithful 3xTF32 scheme.  The distance expressions are
+// the reference's: 1 - <a,b> (ip), max((|b|^2 - 2<a,b>) + |a|^2, 0) (l2).
+//
+// All mbarrier waits are bounded; a wait that runs out raises a status word and
+// the CTA winds down (TMEM is released in every path).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace swb {
+namespace sweep {
+
+constexpr int BM = 128;
+constexpr int ROW_BYTES = 128;   // one 128B swizzle atom of K per row per stage
+constexpr int NTHREADS = 192;
+constexpr int BUF = 16;          // per-row candidate buffer (shared memory)
+constexpr float SELF = 3.4e38f;
+
+enum Mode { MODE_F16 = 0, MODE_TF32X3 = 1 };
+
+template <int MODE>
+struct Cfg;
+template <>
+struct Cfg<MODE_F16> {
+    static constexpr int BN = 256;
+    static constexpr int STAGES = 4;
+    static constexpr int KSUB = 4;              // MMAs of K = 16 per 64-element stage
+    static constexpr int NOPS = 1;              // operand pairs per stage
+    static constexpr uint32_t FMT = 0;          // F16
+};
+template <>
+struct Cfg<MODE_TF32X3> {
+    static constexpr int BN = 128;
+    static constexpr int STAGES = 3;
+    static constexpr int KSUB = 4;              // MMAs of K = 8 per 32-element stage
+    static constexpr int NOPS = 2;              // hi and lo of A and of B
+    static constexpr uint32_t FMT = 2;          // TF32
+};
+
+// -- PTX wrappers ------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+template <int MODE>
+__device__ __forceinline__ void umma(uint32_t dtm, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    if constexpr (MODE == MODE_F16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtm),
+            "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtm),
+            "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+            : "memory");
+    }
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// barrier of the 128 epilogue threads (named barrier 1) that also ANDs a
+// predicate across them, so every epilogue warp takes the same branch
+__device__ __forceinline__ bool epi_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, 128, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)ok)
+        : "memory");
+    return r != 0;
+}
+
+// 64 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// K-major operand, rows of 128 bytes, 128B swizzle: 8-row groups 1024 B apart
+__device__ __forceinline__ uint64_t smem_desc(const void* p) {
+    const uint64_t a = smem_u32(p);
+    return ((a >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+template <int MODE>
+__host__ __device__ constexpr uint32_t instr_desc() {
+    return (1u << 4)                                   // D in fp32
+           | (Cfg<MODE>::FMT << 7) | (Cfg<MODE>::FMT << 10)   // A, B format
+           | (uint32_t(Cfg<MODE>::BN >> 3) << 17)        // N
+           | (uint32_t(BM >> 4) << 24);                  // M
+}
+
+// -- shared memory ---------------------------------------------------------
+
+template <int MODE>
+struct Layout {
+    static constexpr int BN = Cfg<MODE>::BN;
+    static constexpr int A_BYTES = BM * ROW_BYTES;
+    static constexpr int B_BYTES = BN * ROW_BYTES;
+    static constexpr int STAGE = Cfg<MODE>::NOPS * (A_BYTES + B_BYTES);
+    static constexpr int STAGES = Cfg<MODE>::STAGES;
+    static constexpr int RING = STAGES * STAGE;
+    static constexpr int NORMS = RING;                          // float [2][BN]
+    static constexpr int BUFD = NORMS + 2 * BN * 4;             // float [BUF][BM]
+    static constexpr int BUFI = BUFD + BUF * BM * 4;            // int   [BUF][BM]
+    static constexpr int BARS = BUFI + BUF * BM * 4;            // full, empty, accf, acce
+    static constexpr int TMEMP = BARS + (2 * STAGES + 4) * 8;
+    static constexpr int TOTAL = TMEMP + 16;
+    static constexpr int ALLOC = TOTAL + 1024;                  // room to align the ring to 1024
+};
+
+struct Params {
+    int64_t n;          // corpus rows (columns of the sweep)
+    int64_t row0, rows; // the rows swept
+    int dim;
+    int C;
+    int metric;
+    const float* norms; // l2: |x|^2 of every row
+    float* best_d;      // [rows][2][C] ping-pong sorted lists (scratch)
+    int32_t* best_i;
+    int32_t* idx;       // [rows][C] out
+    float* dst;
+    int32_t* status;
+};
+
+// merge this row's buffer (cnt entries) into its sorted best list
+__device__ void flush_row(const Params& P, float* bufd, int* bufi, int t, int& cnt, int& nb, int& pp,
+                          float& thd, int& thi, int64_t lrow) {
+    float kd[BUF];
+    int ki[BUF];
+    for (int s = 0; s < cnt; ++s) {
+        kd[s] = bufd[s * BM + t];
+        ki[s] = bufi[s * BM + t];
+    }
+    for (int s = 1; s < cnt; ++s) {   // insertion sort by (d, id)
+        const float d = kd[s];
+        const int i = ki[s];
+        int u = s - 1;
+        while (u >= 0 && key_lt(d, i, kd[u], ki[u])) {
+            kd[u + 1] = kd[u];
+            ki[u + 1] = ki[u];
+            --u;
+        }
+        kd[u + 1] = d;
+        ki[u + 1] = i;
+    }
+    const int C = P.C;
+    const float* ad = P.best_d + (lrow * 2 + pp) * C;
+    const int* ai = P.best_i + (lrow * 2 + pp) * C;
+    float* od = P.best_d + (lrow * 2 + (pp ^ 1)) * C;
+    int* oi = P.best_i + (lrow * 2 + (pp ^ 1)) * C;
+    int a = 0, b = 0, o = 0;
+    float ca = (nb > 0) ? ad[0] : 0.f;
+    int ci = (nb > 0) ? ai[0] : 0;
+    while (o < C && (a < nb || b < cnt)) {
+        const bool takeA = (b >= cnt) || (a < nb && key_lt(ca, ci, kd[b], ki[b]));
+        if (takeA) {
+            od[o] = ca;
+            oi[o] = ci;
+            ++a;
+            if (a < nb) { ca = ad[a]; ci = ai[a]; }
+        } else {
+            od[o] = kd[b];
+            oi[o] = ki[b];
+            ++b;
+        }
+        ++o;
+    }
+    nb = o;
+    pp ^= 1;
+    cnt = 0;
+    if (nb == C) {
+        thd = od[C - 1];
+        thi = oi[C - 1];
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                            const __grid_constant__ CUtensorMap tmA2,
+                                                            const __grid_constant__ CUtensorMap tmB,
+                                                            const __grid_constant__ CUtensorMap tmB2,
+                                                            const __grid_constant__ Params P) {
+    using Ly = Layout<MODE>;
+    constexpr int BN = Cfg<MODE>::BN;
+    constexpr int STAGES = Cfg<MODE>::STAGES;
+    constexpr int KSUB = Cfg<MODE>::KSUB;
+    constexpr int KELEM = (MODE == MODE_F16) ? 64 : 32;          // K elements per stage
+    constexpr uint32_t IDESC = instr_desc<MODE>();
+    extern __shared__ __align__(1024) char smem_raw[];
+    char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ly::BARS);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accf = empty + STAGES;
+    uint64_t* acce = accf + 2;
+    uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(sm + Ly::TMEMP);
+    float* norms_s = reinterpret_cast<float*>(sm + Ly::NORMS);
+    float* bufd = reinterpret_cast<float*>(sm + Ly::BUFD);
+    int* bufi = reinterpret_cast<int*>(sm + Ly::BUFI);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t rb0 = P.row0 + (int64_t)blockIdx.x * BM;   // first global row of this block
+    const int ntiles = (int)((P.n + BN - 1) / BN);
+    const int ksteps = P.dim / KELEM;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&accf[0], 1);
+        mbar_init(&accf[1], 1);
+        mbar_init(&acce[0], 128);
+        mbar_init(&acce[1], 128);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_ptr, 2 * BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_ptr;
+    __shared__ int s_abort_store;
+    volatile int* s_abort = &s_abort_store;
+    if (threadIdx.x == 0) *s_abort = 0;
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            int it = 0;
+            for (int ct = 0; ct < ntiles && !*s_abort; ++ct) {
+                for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                    const int st = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(&empty[st], ph ^ 1)) { *s_abort = 1; break; }
+                    char* base = sm + st * Ly::STAGE;
+                    mbar_expect_tx(&full[st], Ly::STAGE);
+                    const int k0 = ks * KELEM;
+                    tma_load_2d(base, &tmA, k0, (int)rb0, &full[st]);
+                    tma_load_2d(base + Ly::A_BYTES, &tmB, k0, ct * BN, &full[st]);
+                    if constexpr (MODE == MODE_TF32X3) {
+                        tma_load_2d(base + Ly::A_BYTES + Ly::B_BYTES, &tmA2, k0, (int)rb0, &full[st]);
+                        tma_load_2d(base + 2 * Ly::A_BYTES + Ly::B_BYTES, &tmB2, k0, ct * BN, &full[st]);
+                    }
+                }
+            }
+        }
+        __syncwarp();   // reconverge before the block-wide barrier below
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            int it = 0;
+            for (int ct = 0; ct < ntiles && !*s_abort; ++ct) {
+                const int acc = ct & 1;
+                if (!mbar_wait(&acce[acc], ((ct >> 1) & 1) ^ 1)) { *s_abort = 1; break; }
+                tc_fence_after();
+                const uint32_t dtm = tmem + acc * BN;
+                for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                    const int st = it % STAGES;
+                    if (!mbar_wait(&full[st], (it / STAGES) & 1)) { *s_abort = 1; break; }
+                    tc_fence_after();
+                    const char* base = sm + st * Ly::STAGE;
+                    const char* a_hi = base;
+                    const char* b_hi = base + Ly::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < KSUB; ++k) {
+                        const uint32_t first = (ks == 0 && k == 0) ? 0u : 1u;
+                        umma<MODE>(dtm, smem_desc(a_hi + 32 * k), smem_desc(b_hi + 32 * k), IDESC, first);
+                        if constexpr (MODE == MODE_TF32X3) {
+                            const char* a_lo = base + Ly::A_BYTES + Ly::B_BYTES;
+                            const char* b_lo = base + 2 * Ly::A_BYTES + Ly::B_BYTES;
+                            umma<MODE>(dtm, smem_desc(a_hi + 32 * k), smem_desc(b_lo + 32 * k), IDESC, 1u);
+                            umma<MODE>(dtm, smem_desc(a_lo + 32 * k), smem_desc(b_hi + 32 * k), IDESC, 1u);
+                        }
+                    }
+                    umma_commit(&empty[st]);
+                }
+                umma_commit(&accf[acc]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: thread t owns row t of the block
+        const int q = warp & 3;                      // TMEM lane quarter this warp may read
+        const int t = q * 32 + lane;
+        const int et = threadIdx.x - 64;             // 0..127 among the epilogue threads
+        const int64_t grow = rb0 + t;
+        const int64_t lrow = (int64_t)blockIdx.x * BM + t;   // row within the swept range
+        const bool live = (grow < P.row0 + P.rows) && (grow < P.n);
+        const float an = (P.metric == METRIC_L2 && live) ? P.norms[grow] : 0.f;
+        int cnt = 0, nb = 0, pp = 0;
+        float thd = __int_as_float(0x7f800000);
+        int thi = 0x7fffffff;
+        for (int ct = 0; ct < ntiles; ++ct) {
+            const int acc = ct & 1;
+            if (P.metric == METRIC_L2) {
+                for (int c = et; c < BN; c += 128) {
+                    const int64_t j = (int64_t)ct * BN + c;
+                    norms_s[acc * BN + c] = (j < P.n) ? __ldg(&P.norms[j]) : 0.f;
+                }
+            }
+            const bool ok = mbar_wait(&accf[acc], (ct >> 1) & 1);
+            if (!epi_all(ok && !*s_abort)) {   // also publishes the norms written above
+                *s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            for (int ch = 0; ch < BN / 64; ++ch) {
+                float v[64];
+                __syncwarp();   // tcgen05.ld is .sync.aligned: the warp must be converged
+                tmem_ld64(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 64, v);
+                if (ch == BN / 64 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(&acce[acc]);
+                }
+                if (!live) continue;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const int64_t j = (int64_t)ct * BN + ch * 64 + i;
+                    if (j >= P.n) continue;
+                    float d;
+                    if (P.metric == METRIC_IP) {
+                        d = __fsub_rn(1.f, v[i]);
+                    } else {
+                        d = __fadd_rn(__fsub_rn(norms_s[acc * BN + ch * 64 + i], __fmul_rn(2.f, v[i])), an);
+                        d = d < 0.f ? 0.f : d;
+                    }
+                    if (j == grow) d = SELF;
+                    if (key_lt(d, (int)j, thd, thi)) {
+                        bufd[cnt * BM + t] = d;
+                        bufi[cnt * BM + t] = (int)j;
+                        if (++cnt == BUF) flush_row(P, bufd, bufi, t, cnt, nb, pp, thd, thi, lrow);
+                    }
+                }
+            }
+        }
+        if (live) {
+            if (cnt) flush_row(P, bufd, bufi, t, cnt, nb, pp, thd, thi, lrow);
+            const float* fd = P.best_d + (lrow * 2 + pp) * P.C;
+            const int* fi = P.best_i + (lrow * 2 + pp) * P.C;
+            for (int c = 0; c < P.C; ++c) {
+                const bool okc = c < nb;
+                P.idx[lrow * P.C + c] = okc ? fi[c] : -1;
+                P.dst[lrow * P.C + c] = okc ? fd[c] : __int_as_float(0x7f800000);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (*s_abort && threadIdx.x == 0 && P.status) atomicExch(P.status, ERR_TIMEOUT);
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
+// split fp32 rows into tf32 hi (low 13 mantissa bits cleared after rounding to
+// nearest) and lo = x - hi (exact in fp32)
+__global__ void split_tf32_kernel(const float* __restrict__ X, int64_t count, float* __restrict__ hi,
+                                  float* __restrict__ lo) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const float x = X[i];
+    uint32_t b = __float_as_uint(x);
+    b = (b + 0x1000u) & 0xFFFFE000u;   // round half up on the 13 dropped bits
+    float h = __uint_as_float(b);
+    if (!isfinite(h)) h = x;
+    hi[i] = h;
+    lo[i] = __fsub_rn(x, h);
+}
+
+}  // namespace sweep
+}  // namespace swb
+
+// ===========================================================================
+// host side
+
+using namespace swb;
+using namespace swb::sweep;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D map over [n rows, dim] with a box of `box_rows` rows x 128 bytes
+int make_map(CUtensorMap* m, const void* base, int64_t n, int dim, int esize, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return abi::fail(SWB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const CUtensorMapDataType dt = (esize == 2) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    cuuint64_t dims[2] = {(cuuint64_t)dim, (cuuint64_t)n};
+    cuuint64_t strides[1] = {(cuuint64_t)dim * esize};
+    cuuint32_t box[2] = {(cuuint32_t)(ROW_BYTES / esize), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return abi::fail(SWB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SWB_OK;
+}
+
+template <int MODE>
+int launch_sweep(const void* a_hi, const void* a_lo, int64_t n, int dim, const float* norms, int64_t row0,
+                 int64_t rows, int C, int metric, int32_t* idx, float* dst, void* ws, int32_t* status,
+                 cudaStream_t st) {
+    using Ly = Layout<MODE>;
+    const int esize = (MODE == MODE_F16) ? 2 : 4;
+    CUtensorMap mA, mA2, mB, mB2;
+    int rc = make_map(&mA, a_hi, n, dim, esize, BM);
+    if (!rc) rc = make_map(&mB, a_hi, n, dim, esize, Cfg<MODE>::BN);
+    if (!rc) rc = make_map(&mA2, a_lo ? a_lo : a_hi, n, dim, esize, BM);
+    if (!rc) rc = make_map(&mB2, a_lo ? a_lo : a_hi, n, dim, esize, Cfg<MODE>::BN);
+    if (rc) return rc;
+    Params P;
+    P.n = n;
+    P.row0 = row0;
+    P.rows = rows;
+    P.dim = dim;
+    P.C = C;
+    P.metric = metric;
+    P.norms = norms;
+    P.best_d = reinterpret_cast<float*>(ws);
+    P.best_i = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) + (size_t)((rows + BM - 1) / BM) * BM * 2 * C * 4);
+    P.idx = idx;
+    P.dst = dst;
+    P.status = status;
+    const int smem = Ly::ALLOC;
+    cudaError_t e = cudaFuncSetAttribute(sweep_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute(sweep)");
+    const unsigned blocks = (unsigned)((rows + BM - 1) / BM);
+    sweep_kernel<MODE><<<blocks, NTHREADS, smem, st>>>(mA, mA2, mB, mB2, P);
+    return abi::cuda_check("sweep launch");
+}
+
+}  // namespace
+
+extern "C" uint64_t swb_sweep_workspace(int64_t n, int64_t rows, int C, int x_dtype) {
+    const int64_t padded = (rows + BM - 1) / BM * BM;
+    uint64_t b = (uint64_t)padded * 2 * C * 8;                 // ping-pong best lists
+    if (x_dtype == SWB_F32) b += 2 * (uint64_t)n * 0;          // hi / lo planes are caller-provided
+    (void)n;
+    return b;
+}
+
+extern "C" int swb_split_tf32(const float* X, int64_t count, float* hi, float* lo, void* stream) {
+    if (!X || !hi || !lo) return abi::fail(SWB_ERR_ARG, "null buffer");
+    if (count <= 0) return SWB_OK;
+    split_tf32_kernel<<<(unsigned)((count + 255) / 256), 256, 0, (cudaStream_t)stream>>>(X, count, hi, lo);
+    return abi::cuda_check("split launch");
+}
+
+extern "C" int swb_sweep_topc(const void* X, const void* X_lo, int x_dtype, int64_t n, int dim, const float* norms,
+                              int64_t row0, int64_t rows, int C, int metric, int32_t* idx, float* dst,
+                              void* workspace, uint64_t ws_bytes, int32_t* status, void* stream) {
+    if (!X || !idx || !dst || !workspace) return abi::fail(SWB_ERR_ARG, "null buffer");
+    if (C < 1 || C > 256) return abi::fail(SWB_ERR_ARG, "C must be 1..256");
+    if (rows <= 0) return SWB_OK;
+    if (row0 < 0 || row0 + rows > n) return abi::fail(SWB_ERR_ARG, "row range outside the corpus");
+    if (n >= ((int64_t)1 << 31)) return abi::fail(SWB_ERR_ARG, "at most 2^31 - 1 rows");
+    if (metric == SWB_METRIC_L2 && !norms) return abi::fail(SWB_ERR_ARG, "l2 needs row norms");
+    if (ws_bytes < swb_sweep_workspace(n, rows, C, x_dtype)) return abi::fail(SWB_ERR_ARG, "workspace too small");
+    if (reinterpret_cast<uintptr_t>(X) % 16 || (X_lo && reinterpret_cast<uintptr_t>(X_lo) % 16))
+        return abi::fail(SWB_ERR_ARG, "rows must be 16-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (x_dtype == SWB_F16) {
+        if (dim % 64) return abi::fail(SWB_ERR_ARG, "the tensor-core sweep needs dim %% 64 == 0 for fp16 rows");
+        return launch_sweep<MODE_F16>(X, nullptr, n, dim, norms, row0, rows, C, metric, idx, dst, workspace, status,
+                                      st);
+    }
+    if (!X_lo) return abi::fail(SWB_ERR_ARG, "fp32 rows need their tf32 low parts (swb_split_tf32)");
+    if (dim % 32) return abi::fail(SWB_ERR_ARG, "the tensor-core sweep needs dim %% 32 == 0 for fp32 rows");
+    return launch_sweep<MODE_TF32X3>(X, X_lo, n, dim, norms, row0, rows, C, metric, idx, dst, workspace, status,
+                                     st);
+}

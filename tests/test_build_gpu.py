@@ -42,12 +42,18 @@ def _check_candidates(X, got, want, metric):
     return bad
 
 
-@pytest.mark.parametrize("metric,dtype,C", [(0, np.float32, 64), (1, np.float32, 128), (0, np.float16, 128),
-                                            (1, np.float32, 33)])
-def test_candidates_exact_except_ties(metric, dtype, C):
-    X = cases.build_corpus(3000, 64, seed=5 + metric, metric=metric).astype(dtype)
+@pytest.mark.parametrize("method", ["mma", "gemm"])
+@pytest.mark.parametrize("metric,dtype,C,d", [(0, np.float32, 64, 64), (1, np.float32, 128, 64),
+                                              (0, np.float16, 128, 64), (1, np.float32, 33, 48),
+                                              (1, np.float16, 100, 128), (0, np.float32, 128, 96)])
+def test_candidates_exact_except_ties(method, metric, dtype, C, d):
+    """The candidate sweep (tensor-core kernel with fused selection, and the
+    library-GEMM path) against the exact lists: every position agrees or holds
+    a tie within fp32 noise; self is excluded; lists are ascending."""
+    X = cases.build_corpus(3000, d, seed=5 + metric, metric=metric).astype(dtype)
     Xg = torch.from_numpy(X).to(DEV)
-    idx, dst = B.knn_candidates(Xg, C, chunk=1024, metric="ip" if metric == 0 else "l2", col_chunk=1000)
+    idx, dst = B.knn_candidates(Xg, C, chunk=1024, metric="ip" if metric == 0 else "l2", col_chunk=1000,
+                                method=method)
     Xf = X.astype(np.float32)
     want, wd = O.knn_candidates(Xf, C, metric)
     got = idx.cpu().numpy()
@@ -58,6 +64,17 @@ def test_candidates_exact_except_ties(metric, dtype, C):
     d = dst.cpu().numpy()
     assert (np.diff(d, axis=1) >= 0).all()
     assert not (got == np.arange(X.shape[0])[:, None]).any()
+
+
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_sweep_row_range_and_ragged_edges(dtype):
+    """Rows [r0, r1) of a corpus whose size is no multiple of the tiles: the
+    same lists as the whole sweep's rows r0..r1."""
+    X = cases.build_corpus(1000 + 37, 64, seed=9, metric=1).astype(dtype)
+    Xg = torch.from_numpy(X).to(DEV)
+    full, fd = B.knn_candidates(Xg, 40, metric="l2")
+    part, pd = B.knn_candidates(Xg, 40, metric="l2", rows=(129, 700), row_block=256)
+    assert torch.equal(full[129:700], part) and torch.equal(fd[129:700], pd)
 
 
 @pytest.mark.parametrize("metric", [0, 1])
