@@ -136,6 +136,27 @@ __device__ __forceinline__ void widen16(const __half* p, float* out) {
     }
 }
 
+// a 16-byte chunk held in registers, widened to fp32
+template <typename XT>
+__device__ __forceinline__ void widen_u4(const uint4 v, float* out);
+template <>
+__device__ __forceinline__ void widen_u4<float>(const uint4 v, float* out) {
+    out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+    out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+template <>
+__device__ __forceinline__ void widen_u4<__half>(const uint4 v, float* out) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        union { uint32_t u; __half2 h; } c;
+        c.u = w[i];
+        const float2 f = __half22float2(c.h);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+
 template <int TEAM, typename XT>
 __device__ __forceinline__ float team_partial(const float* __restrict__ sq, const XT* __restrict__ row,
                                               int dim, int metric, int tl) {
@@ -230,6 +251,48 @@ __device__ __forceinline__ float split_partial(const float* __restrict__ sq, con
 #pragma unroll
         for (int j = 0; j < h; ++j) acc[j] = __fadd_rn(acc[j], acc[j + h]);
     return acc[0];
+}
+
+// The TEAM-lane distance with the row read straight from global memory: lane
+// tl issues the loads of up to SEG of its chunks (tl, tl + TEAM, ...) at once,
+// then sums them in order; wider rows take several such segments.
+template <int TEAM, typename XT>
+__device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, const XT* __restrict__ grow,
+                                                  int dim, int metric, int tl) {
+    constexpr int V = VecN<XT>::N;
+    constexpr int SEG = 12;
+    const uint4* r4 = reinterpret_cast<const uint4*>(grow);
+    const int nch = dim / V;
+    float acc = 0.f;
+    for (int s0 = tl; s0 < nch; s0 += TEAM * SEG) {
+        uint4 raw[SEG];
+#pragma unroll
+        for (int u = 0; u < SEG; ++u) {
+            const int c = s0 + u * TEAM;
+            raw[u] = (c < nch) ? __ldg(r4 + c) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < SEG; ++u) {
+            const int c = s0 + u * TEAM;
+            if (c < nch) {
+                float x[V], q[V];
+                widen_u4<XT>(raw[u], x);
+#pragma unroll
+                for (int i = 0; i < V; i += 4) widen16(sq + c * V + i, q + i);
+                if (metric == METRIC_IP) {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], x[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) {
+                        const float df = __fsub_rn(q[i], x[i]);
+                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                    }
+                }
+            }
+        }
+    }
+    return acc;
 }
 
 template <int TP>

@@ -66,6 +66,7 @@ struct Knobs {
     int32_t* out_ids;
     float* out_dist;
     int W, R, warp_bytes, q_shared, cmax;
+    int loader;   // 0: bulk copies into a shared-memory ring; 1: direct loads
 };
 
 __host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
@@ -196,6 +197,33 @@ __device__ __forceinline__ float cache_probe(uint64_t* tab, int Hc, int v, int& 
     return FLT_MAX;
 }
 
+// cache_probe given the outcome of its first compare-and-swap (issued by the
+// caller alongside others): resolves it and probes on after a collision
+__device__ __forceinline__ float cache_probe_rest(uint64_t* tab, int Hc, int v, uint32_t pos,
+                                                  unsigned long long old, int& slot, int& claimed) {
+    const uint32_t mask = (uint32_t)(Hc - 1);
+    const uint32_t key = (uint32_t)(v + 1);
+    const unsigned long long want = ((unsigned long long)key << 32) | FLT_MAX_BITS;
+    for (int p = 0;;) {
+        if (old == 0ull) {
+            slot = (int)pos;
+            claimed = 1;
+            return FLT_MAX;
+        }
+        if ((uint32_t)(old >> 32) == key) {
+            slot = (int)pos;
+            claimed = 0;
+            return __uint_as_float((uint32_t)old);
+        }
+        if (++p >= CPROBE) break;
+        pos = (pos + 1) & mask;
+        old = atomicCAS(reinterpret_cast<unsigned long long*>(&tab[pos]), 0ull, want);
+    }
+    slot = -1;
+    claimed = 0;
+    return FLT_MAX;
+}
+
 __device__ __forceinline__ uint64_t cache_pack(int v, float d) {
     return ((uint64_t)(uint32_t)(v + 1) << 32) | (uint64_t)__float_as_uint(d);
 }
@@ -277,6 +305,31 @@ __device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, 
         if (lane < RPR) {
             const int ni = base + lane + R;
             if (ni < m) issue_row<XT>(K, w, ni);
+        }
+    }
+    __syncwarp();
+    return true;
+}
+
+// The direct-load scorer: 32/TEAM rows per round, each team reading its row
+// from global memory into registers (common.cuh team_partial_ldg).  No ring,
+// no barriers; latency is hidden by the other warps of the SM.
+template <int TEAM, typename XT>
+__device__ bool score_rows_ldg(const Knobs& K, const WarpMem& w, int m, const float* sq, uint64_t* ctab,
+                               int lane) {
+    constexpr int P = 32 / TEAM;
+    const int team = lane / TEAM, tl = lane % TEAM;
+    const XT* X = reinterpret_cast<const XT*>(K.X);
+    for (int base = 0; base < m; base += P) {
+        const int i = base + team;
+        float acc = 0.f;
+        if (i < m) acc = team_partial_ldg<TEAM, XT>(sq, X + (size_t)w.w_v[i] * K.dim, K.dim, K.metric, tl);
+        acc = team_reduce<TEAM>(acc);
+        if (tl == 0 && i < m) {
+            const float d = (K.metric == METRIC_IP) ? __fsub_rn(1.f, acc) : acc;
+            w.w_d[i] = d;
+            const int slot = w.w_slot[i];
+            if (slot >= 0) st_volatile_u64(&ctab[slot], cache_pack(w.w_v[i], d));
         }
     }
     __syncwarp();
@@ -457,7 +510,8 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
     }
     for (int off = 16; off > 0; off >>= 1) fails += __shfl_xor_sync(FULL, fails, off);
     __syncwarp();
-    score_rows<TEAM, TP, XT>(K, w, m, ring, sq, nullptr, lane);
+    if (K.loader) score_rows_ldg<TEAM, XT>(K, w, m, sq, nullptr, lane);
+    else score_rows<TEAM, TP, XT>(K, w, m, ring, sq, nullptr, lane);
     ctr[1] += m;
     ctr[2] += fails;
     for (int t = lane; t < m; t += 32) {
@@ -519,6 +573,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
         int nv[4], nst[4], nsl[4];
         float nd[4];
         int cov = 0, nbr = 0, fails = 0, hits = 0;
+        bool fresh[4];   // passed the visited table; to be probed in the query's table
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
             const int nidx = lane + 32 * t;
@@ -528,34 +583,55 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             nst[t] = 0;   // 0 none, 1 candidate with distance, 2 to be scored
             nsl[t] = -1;
             nd[t] = FLT_MAX;
-            if (v >= 0) {
-                ++nbr;
-                int isnew = 1, fail = 0;
-                if (vis) isnew = visited_insert(vis, K.H, v, fail);
-                fails += fail;
-                if (!isnew) {
-                    ++cov;
-                } else {
-                    int cslot = -1, claimed = 0;
-                    float d = FLT_MAX;
-                    if (ctab) d = cache_probe(ctab, K.Hc, v, cslot, claimed);
-                    // exclusive == 1: a node another branch has scored is off limits
-                    // (local_search.cu:553); exclusive == 2 also treats a claim whose
-                    // distance is still being computed as off limits
-                    const bool taken = K.exclusive && cslot >= 0 && !claimed &&
-                                       (d != FLT_MAX || K.exclusive == 2);
-                    if (taken) {
-                        ++hits;
-                        ++cov;
-                    } else if (d == FLT_MAX) {
-                        nst[t] = 2;
-                        nsl[t] = cslot;
-                    } else {
-                        ++hits;
-                        nst[t] = 1;
-                        nd[t] = d;
-                    }
-                }
+            fresh[t] = false;
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int v = nv[t];
+            if (v < 0) continue;
+            ++nbr;
+            int isnew = 1, fail = 0;
+            if (vis) isnew = visited_insert(vis, K.H, v, fail);
+            fails += fail;
+            if (!isnew) ++cov;
+            else fresh[t] = true;
+        }
+        // The first probe of every fresh neighbour goes out at once (one
+        // compare-and-swap each, independent); only collisions probe on.
+        unsigned long long first_old[4];
+        uint32_t first_pos[4];
+        if (ctab) {
+            const uint32_t cmask = (uint32_t)(K.Hc - 1);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                if (!fresh[t]) continue;
+                const uint32_t key = (uint32_t)(nv[t] + 1);
+                first_pos[t] = knuth(nv[t], cmask);
+                first_old[t] = atomicCAS(reinterpret_cast<unsigned long long*>(&ctab[first_pos[t]]), 0ull,
+                                         ((unsigned long long)key << 32) | FLT_MAX_BITS);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (!fresh[t]) continue;
+            const int v = nv[t];
+            int cslot = -1, claimed = 0;
+            float d = FLT_MAX;
+            if (ctab) d = cache_probe_rest(ctab, K.Hc, v, first_pos[t], first_old[t], cslot, claimed);
+            // exclusive == 1: a node another branch has scored is off limits
+            // (local_search.cu:553); exclusive == 2 also treats a claim whose
+            // distance is still being computed as off limits
+            const bool taken = K.exclusive && cslot >= 0 && !claimed && (d != FLT_MAX || K.exclusive == 2);
+            if (taken) {
+                ++hits;
+                ++cov;
+            } else if (d == FLT_MAX) {
+                nst[t] = 2;
+                nsl[t] = cslot;
+            } else {
+                ++hits;
+                nst[t] = 1;
+                nd[t] = d;
             }
         }
         // rows to score, compacted in slot order
@@ -572,7 +648,9 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             claimed_rows += __popc(__ballot_sync(FULL, nst[t] == 2 && nsl[t] >= 0));
         }
         __syncwarp();
-        if (!score_rows<TEAM, TP, XT>(K, w, m, ring, sq, ctab, lane)) break;
+        const bool scored = K.loader ? score_rows_ldg<TEAM, XT>(K, w, m, sq, ctab, lane)
+                                     : score_rows<TEAM, TP, XT>(K, w, m, ring, sq, ctab, lane);
+        if (!scored) break;
 #pragma unroll
         for (int t = 0; t < 4; ++t)
             if (nst[t] == 2) {
@@ -662,7 +740,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
 // per-warp set-up and state transfer
 
 __device__ __forceinline__ void ring_setup(const Knobs& K, WarpMem& w, int lane, Ring& ring) {
-    if (lane == 0) {
+    if (lane == 0 && K.R > 0) {
         for (int s = 0; s < K.R; ++s) mbar_init(&w.mbar[s], 1);
         fence_mbar_init();
         fence_proxy_async_smem();
@@ -915,12 +993,14 @@ namespace {
 
 int esize_of(int x_dtype) { return x_dtype == 0 ? 4 : 2; }
 
-// Physical lanes per row (common.cuh split_partial): 4 gives 8 rows per round
-// and TEAM/4 add chains per lane; 8 halves the ring a warp needs.  Wide rows
-// default to 8 so that a round's rows fit the staging budget.
+// Physical lanes per row (common.cuh split_partial).  TP = TEAM runs one add
+// chain per lane and 32/TEAM rows per round; TP = 4 or 8 runs TEAM/TP chains
+// per lane and 8 or 4 rows per round, which needs a proportionally deeper ring
+// to keep copies overlapping.  SWB_TP overrides.
 int pick_tp(int rowbytes, int team) {
-    int tp = abi::env_int("SWB_TP", 0);
-    if (tp != 4 && tp != 8) tp = (rowbytes * 8 <= abi::env_int("SWB_RING_BYTES", 12 * 1024)) ? 4 : 8;
+    (void)rowbytes;
+    int tp = abi::env_int("SWB_TP", team);
+    if (tp != 4 && tp != 8 && tp != 16 && tp != 32) tp = team;
     if (tp > team) tp = team;
     return tp;
 }
@@ -985,8 +1065,10 @@ int launch(KernelT kern, dim3 grid, int threads, size_t smem, cudaStream_t st, c
         SWB_CASE(KERNEL, 8, 8, TEAMV, TPV, DT, __VA_ARGS__)                                    \
         SWB_CASE(KERNEL, 16, 4, TEAMV, TPV, DT, __VA_ARGS__)                                   \
         SWB_CASE(KERNEL, 16, 8, TEAMV, TPV, DT, __VA_ARGS__)                                   \
+        SWB_CASE(KERNEL, 16, 16, TEAMV, TPV, DT, __VA_ARGS__)                                  \
         SWB_CASE(KERNEL, 32, 4, TEAMV, TPV, DT, __VA_ARGS__)                                   \
         SWB_CASE(KERNEL, 32, 8, TEAMV, TPV, DT, __VA_ARGS__)                                   \
+        SWB_CASE(KERNEL, 32, 32, TEAMV, TPV, DT, __VA_ARGS__)                                  \
         return abi::fail(SWB_ERR_TEAM, "team_size must be 4, 8, 16 or 32");                   \
     }()
 
@@ -1001,7 +1083,8 @@ int fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int te
     K.rowbytes = dim * esize_of(x_dtype);
     K.L = L;
     const int tp = pick_tp(K.rowbytes, team);
-    K.R = pick_ring(K.rowbytes, tp);
+    K.loader = abi::env_int("SWB_LOADER", 1) ? 1 : 0;
+    K.R = K.loader ? 0 : pick_ring(K.rowbytes, tp);
     K.q_shared = q_shared ? 1 : 0;
     int cm = pow2_at_least(D > V ? D : V);
     const int jq = (J + 3) / 4;
