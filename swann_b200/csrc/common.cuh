@@ -256,11 +256,14 @@ __device__ __forceinline__ float split_partial(const float* __restrict__ sq, con
 // The TEAM-lane distance with the row read straight from global memory: lane
 // tl issues the loads of up to SEG of its chunks (tl, tl + TEAM, ...) at once,
 // then sums them in order; wider rows take several such segments.
+#ifndef SWB_LDG_SEG
+#define SWB_LDG_SEG 6
+#endif
 template <int TEAM, typename XT>
 __device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, const XT* __restrict__ grow,
                                                   int dim, int metric, int tl) {
     constexpr int V = VecN<XT>::N;
-    constexpr int SEG = 12;
+    constexpr int SEG = SWB_LDG_SEG;
     const uint4* r4 = reinterpret_cast<const uint4*>(grow);
     const int nch = dim / V;
     float acc = 0.f;

@@ -883,8 +883,11 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
     for (int t = w + lane; t < k; t += 32) { oi[t] = -1; od[t] = __int_as_float(0x7f800000); }
 }
 
+#ifndef SWB_FUSED_MINB
+#define SWB_FUSED_MINB 4
+#endif
 template <int TEAM, int TP, typename XT>
-__global__ void __launch_bounds__(256) fused_kernel(const __grid_constant__ Knobs K) {
+__global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.y;
@@ -1204,7 +1207,7 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.status = status; K.k = k; K.kk = k < L ? k : L;
     K.branch_ids = branch_ids; K.branch_dist = branch_dist; K.qdone = qdone;
     K.out_ids = out_ids; K.out_dist = out_dist;
-    int W = abi::env_int("SWB_WARPS", 4);
+    int W = abi::env_int("SWB_WARPS", 2);
     if (W > J) W = J;
     if (W < 1) W = 1;
     if (W > 8) W = 8;
