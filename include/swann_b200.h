@@ -129,6 +129,39 @@ SWB_API int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim,
                      int32_t* ids, float* dist, uint8_t* expanded, uint8_t* lineage,
                      int32_t* counters, int32_t* status, void* stream);
 
+/* No counterpart in the reference: the fused search above, for callers that
+ * cannot hand this library device memory for its scratch -- a host runtime
+ * whose memory manager owns the whole device heap and forbids raw cudaMalloc,
+ * or a latency-critical serving thread that must never call an allocator (an
+ * allocation can synchronise the device).  The caller passes only inputs and
+ * outputs; the per-query distance tables, bounds, completion counters,
+ * per-branch result lists and visited tables come from one fixed array of
+ * SWB_STATIC_SCRATCH_BYTES compiled into the library (every GPU that loads the
+ * library holds it until exit).  Nothing is allocated.
+ *   - A configuration needing more scratch than the array holds
+ *     (swb_search_static_bytes) is rejected with SWB_ERR_ARG; split the batch.
+ *   - The first call on a device looks up the array's device address on that
+ *     device (cudaGetSymbolAddress); make that first call before any stream
+ *     capture.
+ *   - Every call shares the one array and clears what must start empty on its
+ *     own stream first.  Calls whose work overlaps on the GPU (other streams,
+ *     other threads) race on the array and corrupt each other's results:
+ *     serialise them.
+ *   - One seed per branch (seeds [Q, J]), POLICY_BEST, no stall or crowd
+ *     rules; shared_cache / shared_bound / exclusive / elide_visited as in
+ *     swb_search_fused; Hc is the per-query table size (a power of two).
+ *   - status (optional) receives SWB_ERR_TIMEOUT if a device wait gave up. */
+#define SWB_STATIC_SCRATCH_BYTES (32u << 20)
+SWB_API int swb_search_fused_static(const void* X, int x_dtype, int64_t n, int dim,
+                            const int32_t* G, int D, const float* Qv, const int32_t* seeds,
+                            int Q, int J, int k, int L, int B, int metric, int team,
+                            float stop_eps, int shared_cache, int shared_bound, int exclusive,
+                            int elide_visited, int Hc, int32_t* out_ids, float* out_dist,
+                            int32_t* status, void* stream);
+/* Scratch bytes swb_search_fused_static needs for a configuration. */
+SWB_API uint64_t swb_search_static_bytes(int Q, int J, int k, int L, int B, int D, int Hc,
+                                 int shared_cache, int exclusive, int elide_visited);
+
 /* ----------------------------------------------------------------- build -- */
 
 /* Replaces the selection half of knn_candidates (swann/build.py:36-42:

@@ -37,6 +37,9 @@ SIGNATURES = {
                                 _i32, _i32, _i32, _f32, _i32, _vp, _i32,
                                 _vp, _i32, _vp, _i32, _i32, _f32,
                                 _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "swb_search_fused_static": (_i32, [_vp, _i32, _i64, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+                                       _i32, _i32, _f32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "swb_search_static_bytes": (_u64, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "swb_topc_block": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _vp, _i32, _vp]),
     "swb_row_norms": (_i32, [_vp, _i32, _i64, _i32, _vp, _vp]),
     "swb_sweep_topc": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _u64,

@@ -1234,3 +1234,109 @@ extern "C" int swb_merge_branches(const int32_t* bids, const float* bdist, int Q
     merge_kernel<<<Q, 256, smem, (cudaStream_t)stream>>>(bids, bdist, n, k, padded, out_ids, out_dist);
     return abi::cuda_check("merge kernel launch");
 }
+
+// ===========================================================================
+// The fused search without caller-provided scratch.
+//
+// Some callers cannot hand this library device buffers for its scratch: a host
+// runtime whose memory manager owns the whole device heap and forbids raw
+// cudaMalloc calls, or a latency-critical serving thread that must never call
+// into an allocator (an allocation can synchronise the device and stall the
+// request).  swb_search_fused_static serves them: it runs the same fused search
+// kernel, but everything the search needs besides its inputs and outputs --
+// per-query distance tables, bounds and completion counters, per-branch result
+// lists, per-branch visited tables -- lives in one fixed array compiled into
+// the library.  It calls no allocation routine of any kind.
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = (size_t)SWB_STATIC_SCRATCH_BYTES;
+
+// Every GPU that loads this library holds this array until the process exits.
+static __device__ __align__(256) unsigned char swb_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_ptr[64] = {nullptr};   // device address of the array, per device ordinal
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// The array's device address on the current device.  The first call on a
+// device looks it up (cudaGetSymbolAddress, with that device current).
+int static_scratch_ptr(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return abi::cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return abi::fail(SWB_ERR_ARG, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, swb_static_scratch);
+        if (e != cudaSuccess) return abi::cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+        g_static_ptr[dev] = p;
+    }
+    *out = g_static_ptr[dev];
+    return SWB_OK;
+}
+
+}  // namespace
+
+extern "C" uint64_t swb_search_static_bytes(int Q, int J, int k, int L, int B, int D, int Hc, int shared_cache,
+                                            int exclusive, int elide_visited) {
+    const int kk = k < L ? k : L;
+    const bool table = shared_cache && J > 1 && Hc > 0;
+    const bool elide = elide_visited && exclusive && table;
+    const int H = elide ? 1 : pow2_at_least(2 * (1 + B * D));
+    size_t b = 0;
+    b += align256((size_t)Q * 4);                           // completion counters
+    b += align256((size_t)Q * 4);                           // bounds
+    b += align256((size_t)Q * J * kk * 4) * 2;              // per-branch ids, distances
+    b += align256((size_t)4);                               // status word
+    if (table) b += align256((size_t)Q * Hc * 8);           // distance tables
+    if (H > 1) b += align256((size_t)Q * J * H * 4);        // visited tables
+    return b;
+}
+
+extern "C" int swb_search_fused_static(const void* X, int x_dtype, int64_t n, int dim, const int32_t* G, int D,
+                                       const float* Qv, const int32_t* seeds, int Q, int J, int k, int L, int B,
+                                       int metric, int team, float stop_eps, int shared_cache, int shared_bound,
+                                       int exclusive, int elide_visited, int Hc, int32_t* out_ids, float* out_dist,
+                                       int32_t* status, void* stream) {
+    if (Q <= 0 || J <= 0) return SWB_OK;
+    if (Hc > 0 && !pow2(Hc)) return abi::fail(SWB_ERR_ARG, "table size must be a power of two");
+    if (k < 1 || L < 1 || B < 1 || D < 1) return abi::fail(SWB_ERR_ARG, "k, L, B and D must be positive");
+    const uint64_t need = swb_search_static_bytes(Q, J, k, L, B, D, Hc, shared_cache, exclusive, elide_visited);
+    if (need > kStaticScratchBytes)
+        return abi::fail(SWB_ERR_ARG,
+                         "this search needs %llu bytes of scratch; the library's fixed scratch holds %llu. "
+                         "Search fewer queries per call or use a smaller table.",
+                         (unsigned long long)need, (unsigned long long)kStaticScratchBytes);
+    void* base = nullptr;
+    int rc = static_scratch_ptr(&base);
+    if (rc) return rc;
+    const int kk = k < L ? k : L;
+    const bool table = shared_cache && J > 1 && Hc > 0;
+    const bool elide = elide_visited && exclusive && table;
+    const int H = elide ? 1 : pow2_at_least(2 * (1 + B * D));
+    char* p = static_cast<char*>(base);
+    int32_t* qdone = reinterpret_cast<int32_t*>(p); p += align256((size_t)Q * 4);
+    float* bound = reinterpret_cast<float*>(p); p += align256((size_t)Q * 4);
+    int32_t* bids = reinterpret_cast<int32_t*>(p); p += align256((size_t)Q * J * kk * 4);
+    float* bdist = reinterpret_cast<float*>(p); p += align256((size_t)Q * J * kk * 4);
+    int32_t* own_status = reinterpret_cast<int32_t*>(p); p += align256((size_t)4);
+    uint64_t* cache = nullptr;
+    if (table) { cache = reinterpret_cast<uint64_t*>(p); p += align256((size_t)Q * Hc * 8); }
+    int32_t* visited = nullptr;
+    if (H > 1) { visited = reinterpret_cast<int32_t*>(p); p += align256((size_t)Q * J * H * 4); }
+    cudaStream_t st = (cudaStream_t)stream;
+    // What a previous call left behind is cleared on this stream first: the
+    // tables, bounds and completion counters must start empty (the visited
+    // tables and branch lists are rewritten by the kernel before use).
+    rc = swb_search_prepare(Q, table ? cache : nullptr, table ? Hc : 0, shared_bound && J > 1 ? bound : nullptr,
+                            qdone, stream);
+    if (rc) return rc;
+    int32_t* stat = status ? status : own_status;
+    return swb_search_fused(X, x_dtype, n, dim, G, D, Qv, seeds, Q, J, 1, k, L, B, metric, team, 0, stop_eps, k,
+                            visited, H, cache, table ? Hc : 0, shared_bound && J > 1 ? bound : nullptr,
+                            table ? exclusive : 0, 0, 0.f, bids, bdist, qdone, out_ids, out_dist, nullptr, nullptr,
+                            nullptr, nullptr, nullptr, stat, st);
+}
