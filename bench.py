@@ -45,6 +45,14 @@ CONFIGS = {
                desc="C1: 10k x 128 fp32 N(0,1) L2 corpus (CPU-runnable case)"),
     "small": dict(n=100_000, d=256, clusters=100, half=True, metric="ip", batch=8192, k=10,
                   desc="small: 100k x 256 fp16 inner-product corpus (smoke-scale)"),
+    # the graph build benchmark (2M x 1024 fp32, L2)
+    "c5": dict(n=2_000_000, d=1024, clusters=1000, half=False, metric="l2", batch=0, k=10,
+               desc="C5: 2M x 1024 fp32 L2 corpus, 1000-component mixture (sigma 0.3)"),
+    # small build shapes for ncu captures (fp16 IP and fp32 L2)
+    "b16s": dict(n=100_000, d=1536, clusters=200, half=True, metric="ip", batch=0, k=10,
+                 desc="build profiling case: 100k x 1536 fp16 inner product"),
+    "b32s": dict(n=100_000, d=1024, clusters=100, half=False, metric="l2", batch=0, k=10,
+                 desc="build profiling case: 100k x 1024 fp32 L2"),
     # C3-shaped profiling case: same row width and mixture model, a corpus
     # (0.6 GB) still larger than L2, small enough for an ncu capture
     "c3s": dict(n=200_000, d=1536, clusters=200, half=True, metric="ip", batch=4096, k=10,
@@ -525,6 +533,49 @@ def run(args):
         dist.destroy_process_group()
 
 
+def run_build(args):
+    """Graph build seconds (sweep / prune / reverse) on one GPU, with the sweep
+    against the tensor pipe: 2 n^2 d FLOPs over the measured dense bf16 peak
+    for fp16 rows (kind::f16), a third of it for fp32 rows (3xTF32 issues three
+    tf32 MMAs per product at half the bf16 rate, so 1/6 of the bf16 peak is the
+    3xTF32 ceiling)."""
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    cfg = dict(CONFIGS[args.config])
+    from swann_b200 import build as B
+    X = make_corpus(cfg, dev)
+    torch.cuda.synchronize()
+    n, d = X.shape
+    t0 = time.perf_counter()
+    cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"])
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"])
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"])
+    torch.cuda.synchronize()
+    t3 = time.perf_counter()
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    flops = 2.0 * n * n * d
+    ceiling = bf16 if cfg["half"] else bf16 / 6.0
+    achieved = flops / (t1 - t0) / 1e12
+    line = {"metric": f"graph build seconds ({cfg['desc']}, degree 64, candidates 128, alpha 1.2)",
+            "value": round(t3 - t0, 3), "unit": "s", "n_gpus": world, "higher_is_better": False,
+            "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
+            "config": {"workload": args.config, "n": n, "d": d, "storage": "f16" if cfg["half"] else "f32",
+                       "metric": cfg["metric"], "sweep": os.environ.get("SWB_SWEEP", "mma")},
+            "stages_s": {"sweep": round(t1 - t0, 3), "prune": round(t2 - t1, 3), "reverse": round(t3 - t2, 3)},
+            "roofline": {"bound": "tensor", "kernel": "swb::sweep::sweep_kernel", "achieved": round(achieved, 1),
+                         "peak": round(ceiling, 1), "unit": "TFLOP/s", "frac": round(achieved / ceiling, 4),
+                         "peak_source": ("measured bf16_tflops" if cfg["half"] else
+                                         "measured bf16_tflops / 6 (3xTF32)"), "flops": flops},
+            "mean_out_degree": round(float((G >= 0).sum(1).float().mean()), 2)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     """The reference's own CPU search path (the C restatement of
     swann/_refcpu.py, independent branches merged) on the host cores, on the
@@ -590,10 +641,13 @@ def main():
     ap.add_argument("--gt", type=int, default=8192)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--fixed", default="", help="branches,queue,stop_eps: skip the calibration")
+    ap.add_argument("--build-only", action="store_true", help="time the graph build instead of the search")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.build_only:
+        run_build(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run(args)

@@ -42,7 +42,7 @@ namespace sweep {
 constexpr int BM = 128;
 constexpr int ROW_BYTES = 128;   // one 128B swizzle atom of K per row per stage
 constexpr int NTHREADS = 192;
-constexpr int BUF = 16;          // per-row candidate buffer (shared memory)
+constexpr int BUF = 24;          // per-row candidate buffer (shared memory), <= 32
 constexpr float SELF = 3.4e38f;
 
 enum Mode { MODE_F16 = 0, MODE_TF32X3 = 1 };
@@ -203,55 +203,120 @@ struct Params {
     int32_t* status;
 };
 
-// merge this row's buffer (cnt entries) into its sorted best list
-__device__ void flush_row(const Params& P, float* bufd, int* bufi, int t, int& cnt, int& nb, int& pp,
-                          float& thd, int& thi, int64_t lrow) {
-    float kd[BUF];
-    int ki[BUF];
-    for (int s = 0; s < cnt; ++s) {
-        kd[s] = bufd[s * BM + t];
-        ki[s] = bufi[s * BM + t];
-    }
-    for (int s = 1; s < cnt; ++s) {   // insertion sort by (d, id)
-        const float d = kd[s];
-        const int i = ki[s];
-        int u = s - 1;
-        while (u >= 0 && key_lt(d, i, kd[u], ki[u])) {
-            kd[u + 1] = kd[u];
-            ki[u + 1] = ki[u];
-            --u;
-        }
-        kd[u + 1] = d;
-        ki[u + 1] = i;
-    }
+// Warp-cooperative merge of row r's buffer (bcnt <= BUF entries, shared memory)
+// into its sorted best list (global, nb entries, C <= 256), written to the other
+// half of the row's ping-pong pair.  The buffer entries are sorted across the
+// warp; lane l holds best entries l*PER .. l*PER+PER-1; every entry's merged
+// position is its own index plus the number of the other list's entries that
+// precede it, so each is stored straight to its place.  Keys are (distance, id)
+// with distinct ids, so no two entries tie.  Returns the merged length; the
+// new C-th entry (when the list is full) comes back in thd / thi on every lane.
+constexpr int PER = 8;
+__device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, int r, int64_t lrow, int bcnt,
+                          int nb, int pp, int lane, float& thd, int& thi) {
     const int C = P.C;
+    float bd = __int_as_float(0x7f800000);
+    int bi = 0x7fffffff;
+    if (lane < bcnt) {
+        bd = bufd[lane * BM + r];
+        bi = bufi[lane * BM + r];
+    }
+    // sort the buffer entries across the warp (bitonic, ascending)
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float pd = __shfl_xor_sync(FULL, bd, j);
+            const int pi = __shfl_xor_sync(FULL, bi, j);
+            const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+            const bool take = (lower == up) ? key_lt(pd, pi, bd, bi) : key_lt(bd, bi, pd, pi);
+            if (take) { bd = pd; bi = pi; }
+        }
+    }
     const float* ad = P.best_d + (lrow * 2 + pp) * C;
     const int* ai = P.best_i + (lrow * 2 + pp) * C;
     float* od = P.best_d + (lrow * 2 + (pp ^ 1)) * C;
     int* oi = P.best_i + (lrow * 2 + (pp ^ 1)) * C;
-    int a = 0, b = 0, o = 0;
-    float ca = (nb > 0) ? ad[0] : 0.f;
-    int ci = (nb > 0) ? ai[0] : 0;
-    while (o < C && (a < nb || b < cnt)) {
-        const bool takeA = (b >= cnt) || (a < nb && key_lt(ca, ci, kd[b], ki[b]));
-        if (takeA) {
-            od[o] = ca;
-            oi[o] = ci;
-            ++a;
-            if (a < nb) { ca = ad[a]; ci = ai[a]; }
-        } else {
-            od[o] = kd[b];
-            oi[o] = ki[b];
-            ++b;
-        }
-        ++o;
+    float ed[PER];
+    int ei[PER], epos[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+        const int idx = lane * PER + u;
+        const bool ok = idx < nb;
+        ed[u] = ok ? ad[idx] : __int_as_float(0x7f800000);
+        ei[u] = ok ? ai[idx] : 0x7fffffff;
+        epos[u] = idx;
     }
-    nb = o;
-    pp ^= 1;
-    cnt = 0;
-    if (nb == C) {
-        thd = od[C - 1];
-        thi = oi[C - 1];
+    int mine = 0;   // best entries preceding this lane's buffer entry
+    for (int s = 0; s < bcnt; ++s) {
+        const float sd = __shfl_sync(FULL, bd, s);
+        const int si = __shfl_sync(FULL, bi, s);
+        int c = 0;
+#pragma unroll
+        for (int u = 0; u < PER; ++u) {
+            if (key_lt(sd, si, ed[u], ei[u])) ++epos[u];
+            else if (lane * PER + u < nb) ++c;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(FULL, c, off);
+        if (lane == s) mine = c;
+    }
+    const int newn = min(C, nb + bcnt);
+    int last = 0;   // this lane wrote position C - 1
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+        if (lane * PER + u < nb && epos[u] < C) {
+            od[epos[u]] = ed[u];
+            oi[epos[u]] = ei[u];
+            if (epos[u] == C - 1) last = 1 + u;
+        }
+    }
+    if (lane < bcnt) {
+        const int pos = lane + mine;
+        if (pos < C) {
+            od[pos] = bd;
+            oi[pos] = bi;
+            if (pos == C - 1) last = 100;
+        }
+    }
+    if (newn == C) {
+        const unsigned w = __ballot_sync(FULL, last != 0);
+        const int src = __ffs(w) - 1;
+        float td = 0.f;
+        int ti = 0;
+        if (lane == src) {
+            if (last == 100) { td = bd; ti = bi; }
+            else { td = ed[last - 1]; ti = ei[last - 1]; }
+        }
+        thd = __shfl_sync(FULL, td, src);
+        thi = __shfl_sync(FULL, ti, src);
+    }
+    return newn;
+}
+
+// flush every row of the warp whose flag is set
+__device__ __forceinline__ void flush_rows(const Params& P, const float* bufd, const int* bufi, int lane, int t,
+                                           int64_t lrow, bool want, int& cnt, int& nb, int& pp, float& thd,
+                                           int& thi) {
+    unsigned m = __ballot_sync(FULL, want);
+    while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        const int r = __shfl_sync(FULL, t, src);
+        const long long lr = __shfl_sync(FULL, (long long)lrow, src);
+        const int bc = __shfl_sync(FULL, cnt, src);
+        const int n0 = __shfl_sync(FULL, nb, src);
+        const int p0 = __shfl_sync(FULL, pp, src);
+        float td = thd;
+        int ti = thi;
+        const int n1 = coop_flush(P, bufd, bufi, r, lr, bc, n0, p0, lane, td, ti);
+        __syncwarp();
+        if (lane == src) {
+            nb = n1;
+            pp ^= 1;
+            cnt = 0;
+            if (n1 == P.C) { thd = td; thi = ti; }
+        }
     }
 }
 
@@ -396,35 +461,43 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                     tc_fence_before();
                     mbar_arrive(&acce[acc]);
                 }
-                if (!live) continue;
 #pragma unroll
                 for (int i = 0; i < 64; ++i) {
                     const int64_t j = (int64_t)ct * BN + ch * 64 + i;
-                    if (j >= P.n) continue;
-                    float d;
-                    if (P.metric == METRIC_IP) {
-                        d = __fsub_rn(1.f, v[i]);
-                    } else {
-                        d = __fadd_rn(__fsub_rn(norms_s[acc * BN + ch * 64 + i], __fmul_rn(2.f, v[i])), an);
-                        d = d < 0.f ? 0.f : d;
+                    if (live && j < P.n) {
+                        float d;
+                        if (P.metric == METRIC_IP) {
+                            d = __fsub_rn(1.f, v[i]);
+                        } else {
+                            d = __fadd_rn(__fsub_rn(norms_s[acc * BN + ch * 64 + i], __fmul_rn(2.f, v[i])), an);
+                            d = d < 0.f ? 0.f : d;
+                        }
+                        if (j == grow) d = SELF;
+                        if (key_lt(d, (int)j, thd, thi)) {
+                            bufd[cnt * BM + t] = d;
+                            bufi[cnt * BM + t] = (int)j;
+                            ++cnt;
+                        }
                     }
-                    if (j == grow) d = SELF;
-                    if (key_lt(d, (int)j, thd, thi)) {
-                        bufd[cnt * BM + t] = d;
-                        bufi[cnt * BM + t] = (int)j;
-                        if (++cnt == BUF) flush_row(P, bufd, bufi, t, cnt, nb, pp, thd, thi, lrow);
-                    }
+                    if (__any_sync(FULL, cnt == BUF))
+                        flush_rows(P, bufd, bufi, lane, t, lrow, cnt == BUF, cnt, nb, pp, thd, thi);
                 }
             }
         }
-        if (live) {
-            if (cnt) flush_row(P, bufd, bufi, t, cnt, nb, pp, thd, thi, lrow);
-            const float* fd = P.best_d + (lrow * 2 + pp) * P.C;
-            const int* fi = P.best_i + (lrow * 2 + pp) * P.C;
-            for (int c = 0; c < P.C; ++c) {
-                const bool okc = c < nb;
-                P.idx[lrow * P.C + c] = okc ? fi[c] : -1;
-                P.dst[lrow * P.C + c] = okc ? fd[c] : __int_as_float(0x7f800000);
+        flush_rows(P, bufd, bufi, lane, t, lrow, live && cnt > 0, cnt, nb, pp, thd, thi);
+        // rows of this warp to the output, one row at a time, coalesced
+        for (int src = 0; src < 32; ++src) {
+            const bool lv = __shfl_sync(FULL, live, src);
+            if (!lv) continue;
+            const long long lr = __shfl_sync(FULL, (long long)lrow, src);
+            const int n1 = __shfl_sync(FULL, nb, src);
+            const int p1 = __shfl_sync(FULL, pp, src);
+            const float* fd = P.best_d + (lr * 2 + p1) * P.C;
+            const int* fi = P.best_i + (lr * 2 + p1) * P.C;
+            for (int c = lane; c < P.C; c += 32) {
+                const bool okc = c < n1;
+                P.idx[lr * P.C + c] = okc ? fi[c] : -1;
+                P.dst[lr * P.C + c] = okc ? fd[c] : __int_as_float(0x7f800000);
             }
         }
     }
@@ -545,7 +618,7 @@ extern "C" int swb_sweep_topc(const void* X, const void* X_lo, int x_dtype, int6
                               int64_t row0, int64_t rows, int C, int metric, int32_t* idx, float* dst,
                               void* workspace, uint64_t ws_bytes, int32_t* status, void* stream) {
     if (!X || !idx || !dst || !workspace) return abi::fail(SWB_ERR_ARG, "null buffer");
-    if (C < 1 || C > 256) return abi::fail(SWB_ERR_ARG, "C must be 1..256");
+    if (C < 1 || C > 32 * PER) return abi::fail(SWB_ERR_ARG, "C must be 1..%d", 32 * PER);
     if (rows <= 0) return SWB_OK;
     if (row0 < 0 || row0 + rows > n) return abi::fail(SWB_ERR_ARG, "row range outside the corpus");
     if (n >= ((int64_t)1 << 31)) return abi::fail(SWB_ERR_ARG, "at most 2^31 - 1 rows");
