@@ -159,7 +159,10 @@ def _knn_mma(Xg, C, metric, half_exact, rows, row_block):
                                     N.ptr(status), s)
             N.check(rc, "knn_candidates")
     if int(status[0]) != 0:
-        raise N.SwannError(int(status[0]), "a device-side wait timed out in the sweep")
+        code = int(status[0])
+        why = ("the sweep's shared memory was not 1024-byte aligned" if code == N.ERR_SMEM
+               else "a device-side wait timed out in the sweep")
+        raise N.SwannError(code, why)
     return idx, dst
 
 

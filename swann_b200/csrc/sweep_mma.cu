@@ -42,7 +42,8 @@ namespace sweep {
 constexpr int BM = 128;
 constexpr int ROW_BYTES = 128;   // one 128B swizzle atom of K per row per stage
 constexpr int NTHREADS = 192;
-constexpr int BUF = 24;          // per-row candidate buffer (shared memory), <= 32
+constexpr int BUF = 31;          // per-row candidate buffer (shared memory), <= 32
+constexpr int GROUP = 16;        // columns filtered between two flush checks
 constexpr float SELF = 3.4e38f;
 
 enum Mode { MODE_F16 = 0, MODE_TF32X3 = 1 };
@@ -133,27 +134,21 @@ __device__ __forceinline__ bool epi_all(bool ok) {
     return r != 0;
 }
 
-// 64 consecutive fp32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
-    uint32_t r[64];
+// 32 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // K-major operand, rows of 128 bytes, 128B swizzle: 8-row groups 1024 B apart
@@ -186,7 +181,7 @@ struct Layout {
     static constexpr int BARS = BUFI + BUF * BM * 4;            // full, empty, accf, acce
     static constexpr int TMEMP = BARS + (2 * STAGES + 4) * 8;
     static constexpr int TOTAL = TMEMP + 16;
-    static constexpr int ALLOC = TOTAL + 1024;                  // room to align the ring to 1024
+    static constexpr int ALLOC = TOTAL;   // the 1024-aligned extern declaration aligns the ring
 };
 
 struct Params {
@@ -203,23 +198,27 @@ struct Params {
     int32_t* status;
 };
 
-// Warp-cooperative merge of row r's buffer (bcnt <= BUF entries, shared memory)
+// Warp-cooperative merge of row r's buffer (bcnt <= 32 entries, shared memory)
 // into its sorted best list (global, nb entries, C <= 256), written to the other
-// half of the row's ping-pong pair.  The buffer entries are sorted across the
-// warp; lane l holds best entries l*PER .. l*PER+PER-1; every entry's merged
-// position is its own index plus the number of the other list's entries that
-// precede it, so each is stored straight to its place.  Keys are (distance, id)
-// with distinct ids, so no two entries tie.  Returns the merged length; the
-// new C-th entry (when the list is full) comes back in thd / thi on every lane.
+// half of the row's ping-pong pair.  The row's own index `self` takes the
+// distance SELF here (the filter lets it through on its true distance, which is
+// at most SELF, so nothing the reference keeps is lost).  The buffer entries
+// are sorted across the warp; lane l holds best entries l*PER .. l*PER+PER-1;
+// every entry's merged position is its own index plus the number of the other
+// list's entries that precede it, so each is stored straight to its place.
+// Keys are (distance, id) with distinct ids, so no two entries tie.  Returns
+// the merged length; when the list is full, the new C-th distance comes back
+// in thd on every lane.
 constexpr int PER = 8;
-__device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, int r, int64_t lrow, int bcnt,
-                          int nb, int pp, int lane, float& thd, int& thi) {
+__device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, int r, int self, int64_t lrow,
+                          int bcnt, int nb, int pp, int lane, float& thd) {
     const int C = P.C;
     float bd = __int_as_float(0x7f800000);
     int bi = 0x7fffffff;
     if (lane < bcnt) {
         bd = bufd[lane * BM + r];
         bi = bufi[lane * BM + r];
+        if (bi == self) bd = SELF;
     }
     // sort the buffer entries across the warp (bitonic, ascending)
 #pragma unroll
@@ -262,13 +261,14 @@ __device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, i
         if (lane == s) mine = c;
     }
     const int newn = min(C, nb + bcnt);
-    int last = 0;   // this lane wrote position C - 1
+    bool last = false;   // this lane wrote position C - 1
+    float lastd = 0.f;
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
         if (lane * PER + u < nb && epos[u] < C) {
             od[epos[u]] = ed[u];
             oi[epos[u]] = ei[u];
-            if (epos[u] == C - 1) last = 1 + u;
+            if (epos[u] == C - 1) { last = true; lastd = ed[u]; }
         }
     }
     if (lane < bcnt) {
@@ -276,47 +276,74 @@ __device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, i
         if (pos < C) {
             od[pos] = bd;
             oi[pos] = bi;
-            if (pos == C - 1) last = 100;
+            if (pos == C - 1) { last = true; lastd = bd; }
         }
     }
     if (newn == C) {
-        const unsigned w = __ballot_sync(FULL, last != 0);
-        const int src = __ffs(w) - 1;
-        float td = 0.f;
-        int ti = 0;
-        if (lane == src) {
-            if (last == 100) { td = bd; ti = bi; }
-            else { td = ed[last - 1]; ti = ei[last - 1]; }
-        }
-        thd = __shfl_sync(FULL, td, src);
-        thi = __shfl_sync(FULL, ti, src);
+        const unsigned w = __ballot_sync(FULL, last);
+        thd = __shfl_sync(FULL, lastd, __ffs(w) - 1);
     }
     return newn;
 }
 
-// flush every row of the warp whose flag is set
-__device__ __forceinline__ void flush_rows(const Params& P, const float* bufd, const int* bufi, int lane, int t,
-                                           int64_t lrow, bool want, int& cnt, int& nb, int& pp, float& thd,
-                                           int& thi) {
+// a row's filter state: buffered entries, best-list length, which half of the
+// ping-pong pair holds the list, and the list's C-th distance (the threshold)
+struct RowState {
+    int cnt, nb, pp;
+    float th;
+};
+
+// flush every row of the warp whose flag is set; kept out of line (state in
+// and out by value) so the filter loop that calls it stays small in the
+// instruction cache
+__device__ __noinline__ RowState flush_rows(const Params& P, const float* bufd, const int* bufi, int lane, int t,
+                                            int64_t lrow, int64_t rb0, bool want, RowState st) {
     unsigned m = __ballot_sync(FULL, want);
     while (m) {
         const int src = __ffs(m) - 1;
         m &= m - 1;
         const int r = __shfl_sync(FULL, t, src);
         const long long lr = __shfl_sync(FULL, (long long)lrow, src);
-        const int bc = __shfl_sync(FULL, cnt, src);
-        const int n0 = __shfl_sync(FULL, nb, src);
-        const int p0 = __shfl_sync(FULL, pp, src);
-        float td = thd;
-        int ti = thi;
-        const int n1 = coop_flush(P, bufd, bufi, r, lr, bc, n0, p0, lane, td, ti);
+        const int bc = __shfl_sync(FULL, st.cnt, src);
+        const int n0 = __shfl_sync(FULL, st.nb, src);
+        const int p0 = __shfl_sync(FULL, st.pp, src);
+        float td = st.th;
+        const int n1 = coop_flush(P, bufd, bufi, r, (int)(rb0 + r), lr, bc, n0, p0, lane, td);
         __syncwarp();
         if (lane == src) {
-            nb = n1;
-            pp ^= 1;
-            cnt = 0;
-            if (n1 == P.C) { thd = td; thi = ti; }
+            st.nb = n1;
+            st.pp ^= 1;
+            st.cnt = 0;
+            if (n1 == P.C) st.th = td;
         }
+    }
+    return st;
+}
+
+// The filter over 16 consecutive columns j0 .. j0+15 of this thread's row:
+// every value below the row's threshold goes to the row's buffer.  Ids already
+// merged into the row's best list are all below j0, so the (distance, id) key
+// order reduces to the distance alone here.  Branch-free: predicated stores.
+// TAIL: only the first `lim` columns lie inside the corpus.
+template <int METRIC, bool TAIL>
+__device__ __forceinline__ void filter16(const float* v, const float* nrm, float an, int j0, int lim, float th,
+                                         int& cnt, float* myd, int* myi) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float d;
+        if (METRIC == METRIC_IP) {
+            d = __fsub_rn(1.f, v[i]);
+        } else {
+            d = __fadd_rn(__fsub_rn(nrm[i], __fmul_rn(2.f, v[i])), an);
+            d = d < 0.f ? 0.f : d;
+        }
+        bool p = d < th;
+        if (TAIL) p = p && i < lim;
+        if (p) {
+            myd[cnt * BM] = d;
+            myi[cnt * BM] = j0 + i;
+        }
+        cnt += p ? 1 : 0;
     }
 }
 
@@ -333,7 +360,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
     constexpr int KELEM = (MODE == MODE_F16) ? 64 : 32;          // K elements per stage
     constexpr uint32_t IDESC = instr_desc<MODE>();
     extern __shared__ __align__(1024) char smem_raw[];
-    char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    char* sm = smem_raw;
+    // the 128B swizzle needs every stage on a 1024-byte boundary; the extern
+    // declaration asks for it, and a block that did not get it stops here
+    // (uniformly, before any barrier or TMEM allocation) with an error status
+    if (smem_u32(sm) & 1023u) {
+        if (threadIdx.x == 0 && P.status) atomicExch(P.status, SWB_ERR_SMEM);
+        return;
+    }
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ly::BARS);
     uint64_t* empty = full + STAGES;
     uint64_t* accf = empty + STAGES;
@@ -436,9 +470,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
         const int64_t lrow = (int64_t)blockIdx.x * BM + t;   // row within the swept range
         const bool live = (grow < P.row0 + P.rows) && (grow < P.n);
         const float an = (P.metric == METRIC_L2 && live) ? P.norms[grow] : 0.f;
-        int cnt = 0, nb = 0, pp = 0;
-        float thd = __int_as_float(0x7f800000);
-        int thi = 0x7fffffff;
+        RowState rs{0, 0, 0, live ? __int_as_float(0x7f800000) : __int_as_float(0xff800000)};
+        float* myd = bufd + t;
+        int* myi = bufi + t;
         for (int ct = 0; ct < ntiles; ++ct) {
             const int acc = ct & 1;
             if (P.metric == METRIC_L2) {
@@ -453,38 +487,36 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                 break;
             }
             tc_fence_after();
-            for (int ch = 0; ch < BN / 64; ++ch) {
-                float v[64];
+            const int cbase = ct * BN;
+            const int lim = (int)(P.n - cbase);   // columns of this tile inside the corpus
+#pragma unroll 1
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                float v[32];
                 __syncwarp();   // tcgen05.ld is .sync.aligned: the warp must be converged
-                tmem_ld64(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 64, v);
-                if (ch == BN / 64 - 1) {
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 32, v);
+                if (ch == BN / 32 - 1) {
                     tc_fence_before();
                     mbar_arrive(&acce[acc]);
                 }
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const int64_t j = (int64_t)ct * BN + ch * 64 + i;
-                    if (live && j < P.n) {
-                        float d;
-                        if (P.metric == METRIC_IP) {
-                            d = __fsub_rn(1.f, v[i]);
-                        } else {
-                            d = __fadd_rn(__fsub_rn(norms_s[acc * BN + ch * 64 + i], __fmul_rn(2.f, v[i])), an);
-                            d = d < 0.f ? 0.f : d;
-                        }
-                        if (j == grow) d = SELF;
-                        if (key_lt(d, (int)j, thd, thi)) {
-                            bufd[cnt * BM + t] = d;
-                            bufi[cnt * BM + t] = (int)j;
-                            ++cnt;
-                        }
+                for (int g = 0; g < 32 / GROUP; ++g) {
+                    const int c0 = ch * 32 + g * GROUP;   // column within the tile
+                    const float* nrm = norms_s + acc * BN + c0;
+                    const int l = lim - c0;
+                    if (P.metric == METRIC_IP) {
+                        if (l >= GROUP) filter16<METRIC_IP, false>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
+                        else filter16<METRIC_IP, true>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
+                    } else {
+                        if (l >= GROUP) filter16<METRIC_L2, false>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
+                        else filter16<METRIC_L2, true>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
                     }
-                    if (__any_sync(FULL, cnt == BUF))
-                        flush_rows(P, bufd, bufi, lane, t, lrow, cnt == BUF, cnt, nb, pp, thd, thi);
+                    const bool full = rs.cnt > BUF - GROUP;
+                    if (__any_sync(FULL, full)) rs = flush_rows(P, bufd, bufi, lane, t, lrow, rb0, full, rs);
                 }
             }
         }
-        flush_rows(P, bufd, bufi, lane, t, lrow, live && cnt > 0, cnt, nb, pp, thd, thi);
+        rs = flush_rows(P, bufd, bufi, lane, t, lrow, rb0, live && rs.cnt > 0, rs);
+        const int nb = rs.nb, pp = rs.pp;
         // rows of this warp to the output, one row at a time, coalesced
         for (int src = 0; src < 32; ++src) {
             const bool lv = __shfl_sync(FULL, live, src);
