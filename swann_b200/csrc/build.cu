@@ -205,69 +205,124 @@ __global__ void __launch_bounds__(256) topc_rows_kernel(const float* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// prune: one block per node.  The C x C Gram matrix of the candidates is built
-// in shared memory (each entry one thread's dimension-ordered fmaf chain), then
-// one warp runs the sequential keep rule.
+// prune: one block per node.  The Gram matrix of the node's (up to 128)
+// candidates is built in shared memory, then one warp runs the sequential keep
+// rule.  Every Gram entry is one thread's dimension-ordered fmaf chain, so the
+// matrix is exactly symmetric and reproducible.
+//
+// Tiling (SIMT, fp32): the 128 x 128 matrix is split over a 16 x 16 thread
+// grid, thread (ty, tx) owning rows {4ty..4ty+3, 64+4ty..64+4ty+3} and the same
+// pattern of columns for tx, so each k step reads its operands as four 16-byte
+// shared loads (conflict-free) for 64 fmaf.  The candidates' rows come in
+// chunks of PR_KC dimensions, transposed into a k-major stage [PR_KC][128]
+// (double-buffered through registers: the next chunk's global loads are in
+// flight while the current one is multiplied).  The stage aliases the Gram
+// array, which is written only after the last chunk.
 
 constexpr int PR_THREADS = 256;
-constexpr int PR_KC = 16;   // dimensions staged per step
+constexpr int PR_KC = 16;    // dimensions staged per chunk
+constexpr int PR_CP = 128;   // candidates per node, padded
+constexpr int PR_GRAM = PR_CP * PR_CP * 4;
+constexpr int PR_SMEM = PR_GRAM + PR_CP * 4 + PR_CP * 4 + PR_CP;
+static_assert(2 * PR_KC * PR_CP * 4 <= PR_GRAM, "the stage must fit in the Gram array");
 
-__global__ void __launch_bounds__(PR_THREADS) prune_kernel(const float* __restrict__ X, int64_t n, int dim,
-                                                          const int32_t* __restrict__ cand,
-                                                          const float* __restrict__ cdist, int C, int deg,
-                                                          float alpha, int metric, int32_t* __restrict__ out) {
+// The next chunk of this thread's two (candidate, 4-dimension) pieces:
+// candidate c = tid & 127, dimensions k0 + 4*kq .. k0 + 4*kq + 3 with
+// kq = (tid >> 7) + 2s.  Dimensions at or past dim read as zero (VEC: dim is a
+// multiple of 4, so a piece is all inside or all outside).
+template <bool VEC>
+__device__ __forceinline__ void prune_fetch(const float* __restrict__ row, int k0, int dim, int kq0, float4 (&pf)[2]) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        const int k = k0 + 4 * (kq0 + 2 * s);
+        if (VEC) {
+            pf[s] = (row && k < dim) ? __ldg(reinterpret_cast<const float4*>(row + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            pf[s].x = (row && k + 0 < dim) ? __ldg(row + k + 0) : 0.f;
+            pf[s].y = (row && k + 1 < dim) ? __ldg(row + k + 1) : 0.f;
+            pf[s].z = (row && k + 2 < dim) ? __ldg(row + k + 2) : 0.f;
+            pf[s].w = (row && k + 3 < dim) ? __ldg(row + k + 3) : 0.f;
+        }
+    }
+}
+
+__device__ __forceinline__ void prune_put(float* stage, int c, int kq0, const float4 (&pf)[2]) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        const int kk = 4 * (kq0 + 2 * s);
+        stage[(kk + 0) * PR_CP + c] = pf[s].x;
+        stage[(kk + 1) * PR_CP + c] = pf[s].y;
+        stage[(kk + 2) * PR_CP + c] = pf[s].z;
+        stage[(kk + 3) * PR_CP + c] = pf[s].w;
+    }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(PR_THREADS, 2) prune_kernel(const float* __restrict__ X, int64_t n, int dim,
+                                                             const int32_t* __restrict__ cand,
+                                                             const float* __restrict__ cdist, int C, int deg,
+                                                             float alpha, int metric, int32_t* __restrict__ out) {
     extern __shared__ __align__(128) char smem[];
-    const int Cp = (C + 15) & ~15;   // padded to the 16 x 16 thread grid
-    float* gram = reinterpret_cast<float*>(smem);                 // [Cp][Cp]
-    float* stage = gram + Cp * Cp;                                 // [PR_KC][Cp]
-    int* cid = reinterpret_cast<int*>(stage + PR_KC * Cp);         // [Cp]
-    float* du = reinterpret_cast<float*>(cid + Cp);                // [Cp]
-    uint8_t* kept = reinterpret_cast<uint8_t*>(du + Cp);           // [Cp]
+    float* gram = reinterpret_cast<float*>(smem);                  // [128][128]
+    float* stage = gram;                                           // [2][PR_KC][128], during the products
+    int* cid = reinterpret_cast<int*>(smem + PR_GRAM);             // [128]
+    float* du = reinterpret_cast<float*>(cid + PR_CP);             // [128]
+    uint8_t* kept = reinterpret_cast<uint8_t*>(du + PR_CP);        // [128]
     const int64_t u = blockIdx.x;
     const int tid = threadIdx.x;
-    for (int i = tid; i < Cp; i += PR_THREADS) {
-        int v = (i < C) ? cand[u * C + i] : -1;
+    if (tid < PR_CP) {
+        const int i = tid;
+        const int v = (i < C) ? cand[u * C + i] : -1;
         cid[i] = (v < n) ? v : -1;   // an id outside the corpus is no candidate
         du[i] = (i < C) ? cdist[u * C + i] : 0.f;
         kept[i] = 0;
     }
     __syncthreads();
-    // thread (ty, tx) owns rows ty + 16a and columns tx + 16b of the Gram matrix
     const int ty = tid >> 4, tx = tid & 15;
-    const int nb = Cp / 16;   // <= 8
+    const int sc = tid & (PR_CP - 1), kq0 = tid >> 7;
+    const float* row = cid[sc] >= 0 ? X + (size_t)cid[sc] * dim : nullptr;
     float acc[8][8];
 #pragma unroll
     for (int a = 0; a < 8; ++a)
 #pragma unroll
         for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+    float4 pf[2];
+    prune_fetch<VEC>(row, 0, dim, kq0, pf);
+    prune_put(stage, sc, kq0, pf);
+    __syncthreads();
+    int buf = 0;
     for (int k0 = 0; k0 < dim; k0 += PR_KC) {
-        // stage[kk][c] = X[cid[c]][k0 + kk]
-        for (int e = tid; e < PR_KC * Cp; e += PR_THREADS) {
-            const int c = e / PR_KC, kk = e % PR_KC;
-            const int v = cid[c];
-            const int k = k0 + kk;
-            stage[kk * Cp + c] = (v >= 0 && k < dim) ? __ldg(&X[(size_t)v * dim + k]) : 0.f;
+        const bool more = k0 + PR_KC < dim;
+        if (more) prune_fetch<VEC>(row, k0 + PR_KC, dim, kq0, pf);
+        const float* st = stage + buf * PR_KC * PR_CP;
+        const int kn = min(PR_KC, dim - k0);   // no products past dim: the chains end exactly there
+#pragma unroll
+        for (int kk = 0; kk < PR_KC; ++kk) {
+            if (kk < kn) {
+                const float4 a0 = *reinterpret_cast<const float4*>(st + kk * PR_CP + 4 * ty);
+                const float4 a1 = *reinterpret_cast<const float4*>(st + kk * PR_CP + 64 + 4 * ty);
+                const float4 b0 = *reinterpret_cast<const float4*>(st + kk * PR_CP + 4 * tx);
+                const float4 b1 = *reinterpret_cast<const float4*>(st + kk * PR_CP + 64 + 4 * tx);
+                const float ra[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float rb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int a = 0; a < 8; ++a)
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(ra[a], rb[b], acc[a][b]);
+            }
         }
-        __syncthreads();
-        const int kn = min(PR_KC, dim - k0);
-        for (int kk = 0; kk < kn; ++kk) {
-            float ra[8], rb[8];
-#pragma unroll
-            for (int a = 0; a < 8; ++a) ra[a] = (a < nb) ? stage[kk * Cp + ty + 16 * a] : 0.f;
-#pragma unroll
-            for (int b = 0; b < 8; ++b) rb[b] = (b < nb) ? stage[kk * Cp + tx + 16 * b] : 0.f;
-#pragma unroll
-            for (int a = 0; a < 8; ++a)
-#pragma unroll
-                for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(ra[a], rb[b], acc[a][b]);
-        }
+        if (more) prune_put(stage + (buf ^ 1) * PR_KC * PR_CP, sc, kq0, pf);
+        buf ^= 1;
         __syncthreads();
     }
+    // the stage is dead (the barrier above ends its last reads): write the Gram
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
-#pragma unroll
-        for (int b = 0; b < 8; ++b)
-            if (a < nb && b < nb) gram[(ty + 16 * a) * Cp + tx + 16 * b] = acc[a][b];
+    for (int a = 0; a < 8; ++a) {
+        const int r = (a < 4) ? 4 * ty + a : 64 + 4 * ty + (a - 4);
+        *reinterpret_cast<float4*>(gram + r * PR_CP + 4 * tx) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+        *reinterpret_cast<float4*>(gram + r * PR_CP + 64 + 4 * tx) =
+            make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
+    }
     __syncthreads();
     if (tid < 32) {
         const int lane = tid;
@@ -275,15 +330,15 @@ __global__ void __launch_bounds__(PR_THREADS) prune_kernel(const float* __restri
         for (int i = 0; i < C && nk < deg; ++i) {
             if (cid[i] < 0) continue;
             bool viol = false;
-            const float gii = gram[i * Cp + i];
+            const float gii = gram[i * PR_CP + i];
             for (int j = lane; j < i; j += 32) {
                 if (!kept[j]) continue;
-                const float g = gram[j * Cp + i];
+                const float g = gram[i * PR_CP + j];   // = gram[j][i]: the same chain
                 float pr;
                 if (metric == METRIC_IP) {
                     pr = __fsub_rn(1.f, g);
                 } else {
-                    pr = __fadd_rn(__fsub_rn(gii, __fmul_rn(2.f, g)), gram[j * Cp + j]);
+                    pr = __fadd_rn(__fsub_rn(gii, __fmul_rn(2.f, g)), gram[j * PR_CP + j]);
                     if (pr < 0.f) pr = 0.f;
                 }
                 if (__fmul_rn(alpha, pr) <= du[i]) viol = true;
@@ -461,22 +516,23 @@ size_t radix_temp_bytes(int64_t total) {
     return bytes;
 }
 
-int prune_smem(int C) {
-    const int Cp = (C + 15) & ~15;
-    return Cp * Cp * 4 + PR_KC * Cp * 4 + Cp * 4 + Cp * 4 + Cp;
+// n rows of candidates over a corpus of nx rows
+template <bool VEC>
+int launch_prune_t(const float* X, int64_t nx, int64_t n, int dim, const int32_t* cand, const float* cdist, int C,
+                   int deg, float alpha, int metric, int32_t* out, cudaStream_t st) {
+    if (PR_SMEM > abi::max_smem_optin()) return abi::fail(SWB_ERR_SMEM, "prune needs %d B of shared memory", PR_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(prune_kernel<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM);
+    if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute(prune)");
+    prune_kernel<VEC><<<(unsigned)n, PR_THREADS, PR_SMEM, st>>>(X, nx, dim, cand, cdist, C, deg, alpha, metric, out);
+    return abi::cuda_check("prune launch");
 }
 
-// n rows of candidates over a corpus of nx rows
 int launch_prune(const float* X, int64_t nx, int64_t n, int dim, const int32_t* cand, const float* cdist, int C,
                  int deg, float alpha, int metric, int32_t* out, cudaStream_t st) {
-    const int smem = prune_smem(C);
-    if (smem > abi::max_smem_optin()) return abi::fail(SWB_ERR_SMEM, "prune needs %d B of shared memory", smem);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute(prune)");
-    }
-    prune_kernel<<<(unsigned)n, PR_THREADS, smem, st>>>(X, nx, dim, cand, cdist, C, deg, alpha, metric, out);
-    return abi::cuda_check("prune launch");
+    if (C > PR_CP) return abi::fail(SWB_ERR_ARG, "candidates per node must be at most %d", PR_CP);
+    const bool vec = (dim % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0);
+    return vec ? launch_prune_t<true>(X, nx, n, dim, cand, cdist, C, deg, alpha, metric, out, st)
+               : launch_prune_t<false>(X, nx, n, dim, cand, cdist, C, deg, alpha, metric, out, st);
 }
 
 }  // namespace
