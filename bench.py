@@ -536,9 +536,10 @@ def run(args):
 def run_build(args):
     """Graph build seconds (sweep / prune / reverse) on one GPU, with the sweep
     against the tensor pipe: 2 n^2 d FLOPs over the measured dense bf16 peak
-    for fp16 rows (kind::f16), a third of it for fp32 rows (3xTF32 issues three
-    tf32 MMAs per product at half the bf16 rate, so 1/6 of the bf16 peak is the
-    3xTF32 ceiling)."""
+    for fp16 rows (kind::f16), a sixth of it for fp32 rows (3xTF32 issues three
+    tf32 MMAs per product at half the bf16 rate).  The sweep runs for seconds
+    under the 1 kW power cap, so the denominator is the sustained GEMM figure;
+    the fraction of the burst figure is reported beside it."""
     world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
     cfg = dict(CONFIGS[args.config])
@@ -546,10 +547,11 @@ def run_build(args):
     X = make_corpus(cfg, dev)
     torch.cuda.synchronize()
     n, d = X.shape
-    t0 = time.perf_counter()
-    cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"])
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"])
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
     G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"])
     torch.cuda.synchronize()
     t2 = time.perf_counter()
@@ -557,9 +559,11 @@ def run_build(args):
     torch.cuda.synchronize()
     t3 = time.perf_counter()
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    burst = float(peaks.get("bf16_tflops", 1590.0))
+    sustained = float(peaks.get("bf16_tflops_sustained", 1400.0))
     flops = 2.0 * n * n * d
-    ceiling = bf16 if cfg["half"] else bf16 / 6.0
+    div = 1.0 if cfg["half"] else 6.0
+    ceiling = sustained / div
     achieved = flops / (t1 - t0) / 1e12
     line = {"metric": f"graph build seconds ({cfg['desc']}, degree 64, candidates 128, alpha 1.2)",
             "value": round(t3 - t0, 3), "unit": "s", "n_gpus": world, "higher_is_better": False,
@@ -569,8 +573,10 @@ def run_build(args):
             "stages_s": {"sweep": round(t1 - t0, 3), "prune": round(t2 - t1, 3), "reverse": round(t3 - t2, 3)},
             "roofline": {"bound": "tensor", "kernel": "swb::sweep::sweep_kernel", "achieved": round(achieved, 1),
                          "peak": round(ceiling, 1), "unit": "TFLOP/s", "frac": round(achieved / ceiling, 4),
-                         "peak_source": ("measured bf16_tflops" if cfg["half"] else
-                                         "measured bf16_tflops / 6 (3xTF32)"), "flops": flops},
+                         "peak_source": ("measured bf16_tflops_sustained" if cfg["half"] else
+                                         "measured bf16_tflops_sustained / 6 (3xTF32)"),
+                         "frac_of_burst": round(achieved / (burst / div), 4), "flops": flops},
+            "clocks_during_sweep": clk.summary(),
             "mean_out_degree": round(float((G >= 0).sum(1).float().mean()), 2)}
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -75,6 +75,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended (it issues nothing) until the phase completes or about `ns`
+// nanoseconds pass, instead of returning at once to spin
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for phase `parity` of `bar` to complete: gives up after about
 // two seconds of SM clock and returns false (the caller records a status).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
@@ -83,6 +98,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     for (;;) {
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
+        if (clock64() - t0 > (1ll << 32)) return false;
+    }
+}
+
+// The same bound, with the waiting thread suspended between checks (for
+// warps that share a scheduler with warps doing work).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (clock64() - t0 > (1ll << 32)) return false;
     }
 }

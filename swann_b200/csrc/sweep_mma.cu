@@ -198,22 +198,41 @@ struct Params {
     int32_t* status;
 };
 
-// Warp-cooperative merge of row r's buffer (bcnt <= 32 entries, shared memory)
-// into its sorted best list (global, nb entries, C <= 256), written to the other
-// half of the row's ping-pong pair.  The row's own index `self` takes the
-// distance SELF here (the filter lets it through on its true distance, which is
-// at most SELF, so nothing the reference keeps is lost).  The buffer entries
-// are sorted across the warp; lane l holds best entries l*PER .. l*PER+PER-1;
-// every entry's merged position is its own index plus the number of the other
-// list's entries that precede it, so each is stored straight to its place.
-// Keys are (distance, id) with distinct ids, so no two entries tie.  Returns
-// the merged length; when the list is full, the new C-th distance comes back
-// in thd on every lane.
-constexpr int PER = 8;
+// Warp-cooperative merge of row r's buffer (bcnt <= BUF entries, shared
+// memory) into its sorted best list (global, nb entries, C <= 32 * PER),
+// written to the other half of the row's ping-pong pair.  The row's own index
+// `self` takes the distance SELF here (the filter lets it through on its true
+// distance, which is at most SELF, so nothing the reference keeps is lost).
+//
+// Lane l holds list entries l*PER .. l*PER+PER-1 (loaded first, so the loads
+// overlap the buffer sort); the buffer is sorted across the lanes.  Keys are
+// (distance, id) with distinct ids, so no two entries tie, and every entry's
+// merged position is its own index plus the number of entries of the other
+// sequence before it, found by binary lifting over the lanes:
+//   list entry   -> over the sorted buffer lanes;
+//   buffer entry -> over the lanes' last list entries, then inside one lane.
+// Returns the merged length; when the list is full, the new C-th distance
+// comes back in thd on every lane.
+constexpr int PER_MAX = 8;   // C <= 256
+template <int PER>
 __device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, int r, int self, int64_t lrow,
                           int bcnt, int nb, int pp, int lane, float& thd) {
     const int C = P.C;
-    float bd = __int_as_float(0x7f800000);
+    const float INF = __int_as_float(0x7f800000);
+    const float* ad = P.best_d + (lrow * 2 + pp) * C;
+    const int* ai = P.best_i + (lrow * 2 + pp) * C;
+    float* od = P.best_d + (lrow * 2 + (pp ^ 1)) * C;
+    int* oi = P.best_i + (lrow * 2 + (pp ^ 1)) * C;
+    float ed[PER];
+    int ei[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+        const int idx = lane * PER + u;
+        const bool ok = idx < nb;
+        ed[u] = ok ? ad[idx] : INF;
+        ei[u] = ok ? ai[idx] : 0x7fffffff;
+    }
+    float bd = INF;
     int bi = 0x7fffffff;
     if (lane < bcnt) {
         bd = bufd[lane * BM + r];
@@ -232,43 +251,62 @@ __device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, i
             if (take) { bd = pd; bi = pi; }
         }
     }
-    const float* ad = P.best_d + (lrow * 2 + pp) * C;
-    const int* ai = P.best_i + (lrow * 2 + pp) * C;
-    float* od = P.best_d + (lrow * 2 + (pp ^ 1)) * C;
-    int* oi = P.best_i + (lrow * 2 + (pp ^ 1)) * C;
-    float ed[PER];
-    int ei[PER], epos[PER];
+    // list entries: buffer entries before each (lanes >= bcnt hold +inf)
+    int epos[PER];
 #pragma unroll
-    for (int u = 0; u < PER; ++u) {
-        const int idx = lane * PER + u;
-        const bool ok = idx < nb;
-        ed[u] = ok ? ad[idx] : __int_as_float(0x7f800000);
-        ei[u] = ok ? ai[idx] : 0x7fffffff;
-        epos[u] = idx;
-    }
-    int mine = 0;   // best entries preceding this lane's buffer entry
-    for (int s = 0; s < bcnt; ++s) {
-        const float sd = __shfl_sync(FULL, bd, s);
-        const int si = __shfl_sync(FULL, bi, s);
-        int c = 0;
+    for (int u = 0; u < PER; ++u) epos[u] = 0;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1) {
 #pragma unroll
         for (int u = 0; u < PER; ++u) {
-            if (key_lt(sd, si, ed[u], ei[u])) ++epos[u];
-            else if (lane * PER + u < nb) ++c;
+            const int m = epos[u] + step - 1;
+            const float pd = __shfl_sync(FULL, bd, m);
+            const int pi = __shfl_sync(FULL, bi, m);
+            if (key_lt(pd, pi, ed[u], ei[u])) epos[u] += step;
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(FULL, c, off);
-        if (lane == s) mine = c;
     }
-    const int newn = min(C, nb + bcnt);
-    bool last = false;   // this lane wrote position C - 1
-    float lastd = 0.f;
+    {   // the 32nd buffer lane (only reachable when every lane is a real entry)
+        const float pd = __shfl_sync(FULL, bd, 31);
+        const int pi = __shfl_sync(FULL, bi, 31);
+#pragma unroll
+        for (int u = 0; u < PER; ++u)
+            if (epos[u] == 31 && key_lt(pd, pi, ed[u], ei[u])) epos[u] = 32;
+    }
+    // buffer entries: whole lanes of the list before it, then entries of the next lane
+    const float lastd = ed[PER - 1];
+    const int lasti = ei[PER - 1];
+    int lb = 0;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1) {
+        const int m = lb + step - 1;
+        const float pd = __shfl_sync(FULL, lastd, m);
+        const int pi = __shfl_sync(FULL, lasti, m);
+        if (key_lt(pd, pi, bd, bi)) lb += step;
+    }
+    {
+        const float pd = __shfl_sync(FULL, lastd, 31);
+        const int pi = __shfl_sync(FULL, lasti, 31);
+        if (lb == 31 && key_lt(pd, pi, bd, bi)) lb = 32;
+    }
+    const int src = lb < 32 ? lb : 31;
+    int inlane = 0;
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
-        if (lane * PER + u < nb && epos[u] < C) {
-            od[epos[u]] = ed[u];
-            oi[epos[u]] = ei[u];
-            if (epos[u] == C - 1) { last = true; lastd = ed[u]; }
+        const float pd = __shfl_sync(FULL, ed[u], src);
+        const int pi = __shfl_sync(FULL, ei[u], src);
+        if (lb < 32 && key_lt(pd, pi, bd, bi)) ++inlane;
+    }
+    const int mine = lb * PER + inlane;
+    const int newn = min(C, nb + bcnt);
+    bool last = false;   // this lane wrote position C - 1
+    float lastw = 0.f;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+        const int pos = lane * PER + u + epos[u];
+        if (lane * PER + u < nb && pos < C) {
+            od[pos] = ed[u];
+            oi[pos] = ei[u];
+            if (pos == C - 1) { last = true; lastw = ed[u]; }
         }
     }
     if (lane < bcnt) {
@@ -276,12 +314,12 @@ __device__ int coop_flush(const Params& P, const float* bufd, const int* bufi, i
         if (pos < C) {
             od[pos] = bd;
             oi[pos] = bi;
-            if (pos == C - 1) { last = true; lastd = bd; }
+            if (pos == C - 1) { last = true; lastw = bd; }
         }
     }
     if (newn == C) {
         const unsigned w = __ballot_sync(FULL, last);
-        thd = __shfl_sync(FULL, lastd, __ffs(w) - 1);
+        thd = __shfl_sync(FULL, lastw, __ffs(w) - 1);
     }
     return newn;
 }
@@ -308,7 +346,8 @@ __device__ __noinline__ RowState flush_rows(const Params& P, const float* bufd, 
         const int n0 = __shfl_sync(FULL, st.nb, src);
         const int p0 = __shfl_sync(FULL, st.pp, src);
         float td = st.th;
-        const int n1 = coop_flush(P, bufd, bufi, r, (int)(rb0 + r), lr, bc, n0, p0, lane, td);
+        const int n1 = (P.C <= 128) ? coop_flush<4>(P, bufd, bufi, r, (int)(rb0 + r), lr, bc, n0, p0, lane, td)
+                                    : coop_flush<PER_MAX>(P, bufd, bufi, r, (int)(rb0 + r), lr, bc, n0, p0, lane, td);
         __syncwarp();
         if (lane == src) {
             st.nb = n1;
@@ -323,27 +362,40 @@ __device__ __noinline__ RowState flush_rows(const Params& P, const float* bufd, 
 // The filter over 16 consecutive columns j0 .. j0+15 of this thread's row:
 // every value below the row's threshold goes to the row's buffer.  Ids already
 // merged into the row's best list are all below j0, so the (distance, id) key
-// order reduces to the distance alone here.  Branch-free: predicated stores.
-// TAIL: only the first `lim` columns lie inside the corpus.
+// order reduces to the distance alone here.  The 16 distances and the keep
+// mask are independent of one another; the stores happen only when some lane
+// of the warp keeps a value, each at cnt + (kept values before it), written in
+// column order so that a discarded value's store is overwritten by the next
+// kept one (positions stay below cnt + 16 <= BUF: a group starts at
+// cnt <= BUF - GROUP).  TAIL: only the first `lim` columns lie inside the
+// corpus.
 template <int METRIC, bool TAIL>
 __device__ __forceinline__ void filter16(const float* v, const float* nrm, float an, int j0, int lim, float th,
                                          int& cnt, float* myd, int* myi) {
+    float d[16];
+    unsigned lo = 0, hi = 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        float d;
         if (METRIC == METRIC_IP) {
-            d = __fsub_rn(1.f, v[i]);
+            d[i] = __fsub_rn(1.f, v[i]);
         } else {
-            d = __fadd_rn(__fsub_rn(nrm[i], __fmul_rn(2.f, v[i])), an);
-            d = d < 0.f ? 0.f : d;
+            float e = __fadd_rn(__fsub_rn(nrm[i], __fmul_rn(2.f, v[i])), an);
+            d[i] = e < 0.f ? 0.f : e;
         }
-        bool p = d < th;
+        bool p = d[i] < th;
         if (TAIL) p = p && i < lim;
-        if (p) {
-            myd[cnt * BM] = d;
-            myi[cnt * BM] = j0 + i;
+        if (i < 8) lo |= (p ? 1u : 0u) << i;
+        else hi |= (p ? 1u : 0u) << (i - 8);
+    }
+    const unsigned m = lo | (hi << 8);
+    if (__any_sync(FULL, m != 0)) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int pos = cnt + __popc(m & ((1u << i) - 1u));
+            myd[pos * BM] = d[i];
+            myi[pos * BM] = j0 + i;
         }
-        cnt += p ? 1 : 0;
+        cnt += __popc(m);
     }
 }
 
@@ -414,7 +466,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                 for (int ks = 0; ks < ksteps; ++ks, ++it) {
                     const int st = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&empty[st], ph ^ 1)) { *s_abort = 1; break; }
+                    if (!mbar_wait_sleep(&empty[st], ph ^ 1)) { *s_abort = 1; break; }
                     char* base = sm + st * Ly::STAGE;
                     mbar_expect_tx(&full[st], Ly::STAGE);
                     const int k0 = ks * KELEM;
@@ -434,12 +486,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
             int it = 0;
             for (int ct = 0; ct < ntiles && !*s_abort; ++ct) {
                 const int acc = ct & 1;
-                if (!mbar_wait(&acce[acc], ((ct >> 1) & 1) ^ 1)) { *s_abort = 1; break; }
+                if (!mbar_wait_sleep(&acce[acc], ((ct >> 1) & 1) ^ 1)) { *s_abort = 1; break; }
                 tc_fence_after();
                 const uint32_t dtm = tmem + acc * BN;
                 for (int ks = 0; ks < ksteps; ++ks, ++it) {
                     const int st = it % STAGES;
-                    if (!mbar_wait(&full[st], (it / STAGES) & 1)) { *s_abort = 1; break; }
+                    if (!mbar_wait_sleep(&full[st], (it / STAGES) & 1)) { *s_abort = 1; break; }
                     tc_fence_after();
                     const char* base = sm + st * Ly::STAGE;
                     const char* a_hi = base;
@@ -481,7 +533,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                     norms_s[acc * BN + c] = (j < P.n) ? __ldg(&P.norms[j]) : 0.f;
                 }
             }
-            const bool ok = mbar_wait(&accf[acc], (ct >> 1) & 1);
+            const bool ok = mbar_wait_sleep(&accf[acc], (ct >> 1) & 1);
             if (!epi_all(ok && !*s_abort)) {   // also publishes the norms written above
                 *s_abort = 1;
                 break;
@@ -650,7 +702,7 @@ extern "C" int swb_sweep_topc(const void* X, const void* X_lo, int x_dtype, int6
                               int64_t row0, int64_t rows, int C, int metric, int32_t* idx, float* dst,
                               void* workspace, uint64_t ws_bytes, int32_t* status, void* stream) {
     if (!X || !idx || !dst || !workspace) return abi::fail(SWB_ERR_ARG, "null buffer");
-    if (C < 1 || C > 32 * PER) return abi::fail(SWB_ERR_ARG, "C must be 1..%d", 32 * PER);
+    if (C < 1 || C > 32 * PER_MAX) return abi::fail(SWB_ERR_ARG, "C must be 1..%d", 32 * PER_MAX);
     if (rows <= 0) return SWB_OK;
     if (row0 < 0 || row0 + rows > n) return abi::fail(SWB_ERR_ARG, "row range outside the corpus");
     if (n >= ((int64_t)1 << 31)) return abi::fail(SWB_ERR_ARG, "at most 2^31 - 1 rows");
