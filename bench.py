@@ -397,7 +397,9 @@ def run(args):
         op = box[0]
 
     # Size the per-query distance table from what the queries actually claim:
-    # four times the busiest query's claims (load <= 25%), a power of two.
+    # twice the busiest query's claims (load <= 50% for that query, a few
+    # percent for a typical one), a power of two.  A probe run that finds no
+    # slot scores the row uncached, so a fuller table costs dedup, not results.
     ent = S.select_nearest(Q[:gt_n], index._cat, op["branches"], metric=index._m)
     sd = index.catalogue[ent].to(torch.int32)
     _, _, ctr, _ = E.search_fused_lean(X, G, Q[:gt_n], sd, k=cfg["k"], L=op["queue"], B=64, metric=index._m,
@@ -405,7 +407,7 @@ def run(args):
                                        shared_bound=True, exclusive=2, elide_visited=True)
     claims = (ctr[..., 5].to(torch.int64).sum(1) + op["branches"]).max().item()
     ref_slots = E.cache_size(op["branches"], 64, G.shape[1])
-    slots = min(ref_slots, max(4096, E.next_pow2(4 * int(claims))))
+    slots = min(ref_slots, max(4096, E.next_pow2(2 * int(claims))))
     index.table_slots = slots
     table = {"slots": slots, "reference_slots": ref_slots, "max_claims_per_query": int(claims),
              "max_load": round(claims / slots, 4)}

@@ -102,6 +102,17 @@ SWB_API int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim,
 SWB_API int swb_merge_branches(const int32_t* bids, const float* bdist, int Q, int J, int kk, int k,
                        int32_t* out_ids, float* out_dist, void* stream);
 
+/* Replaces the torch.topk calls of select_nearest (swann/_select.py:93-130):
+ * folds one slice of query x catalogue scores (scores[r * ld + c], catalogue
+ * entries col0 .. col0+P-1) into each query's running E nearest, by the
+ * reference's metric expressions (1 - s; (|v|^2 - 2s) + |q|^2 with vnorm [P]
+ * and qnorm [rows]).  best_d / best_i [rows][E] hold the list sorted by
+ * (distance, index), padding (+inf, -1); resume = 0 starts them fresh.
+ * E <= 128. */
+SWB_API int swb_select_topk(const float* scores, int64_t rows, int P, int64_t ld, const float* vnorm,
+                    const float* qnorm, int metric, int E, int col0, float* best_d, int64_t* best_i,
+                    int resume, void* stream);
+
 /* Clears what a fused search shares per query: the distance table, the bound
  * and the per-query completion counter.  Launch before swb_search_fused on the
  * same stream.  Part of replacing init_kernel's clears (local_search.cu:302-313). */

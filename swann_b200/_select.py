@@ -3,9 +3,9 @@
 Drop-in for swann/_select.py (geniussyn/SWANN:54-128): `pool_vectors`,
 `catalog_scores`, `select_nearest` and `reduced_precision`, same arithmetic --
 a TF32 matmul of the queries against the catalogue rows in slices of 8192,
-turned into the corpus metric, with a running top-E.  The matmul is a plain
-library GEMM (cuBLAS through torch); its output only chooses starting points,
-and the search re-scores everything exactly.
+turned into the corpus metric, with a running top-E (swb_select_topk).  The
+matmul is a plain library GEMM (cuBLAS through torch); its output only chooses
+starting points, and the search re-scores everything exactly.
 """
 from __future__ import annotations
 
@@ -49,12 +49,21 @@ def catalog_scores(Qg, Xg, pool_t, metric=METRIC_IP, Vp=None, precision="tf32"):
 
 
 def select_nearest(Qg, Vp, E, metric=METRIC_IP, precision="tf32", slice_P=8192):
-    """Indices (into the catalogue) of the E nearest entries per query,
-    scored a slice of the catalogue at a time and folded into a running best."""
+    """Indices (into the catalogue) of the E nearest entries per query, sorted
+    nearest first: the catalogue is scored a slice at a time (a library GEMM,
+    the reference's precision choices) and each slice folded into a running
+    best by swb_select_topk, which reads the scores once and keeps the list in
+    shared memory (the reference runs two torch.topk per slice).  Same entries
+    as the reference, up to the order of exactly equal distances."""
+    from . import _lib as N
     n, P = Qg.shape[0], Vp.shape[0]
-    bi = torch.empty(n, 0, dtype=torch.long, device=Qg.device)
-    bv = torch.empty(n, 0, dtype=Qg.dtype, device=Qg.device)
-    qn = (Qg * Qg).sum(1).view(-1, 1) if metric != METRIC_IP else None
+    Ee = min(int(E), P)
+    bd = torch.empty((n, Ee), dtype=torch.float32, device=Qg.device)
+    bi = torch.empty((n, Ee), dtype=torch.int64, device=Qg.device)
+    if n == 0 or Ee == 0:
+        return bi
+    qn = (Qg * Qg).sum(1).contiguous() if metric != METRIC_IP else None
+    stream = N.stream_of(Qg)
     for s in range(0, P, slice_P):
         V = Vp[s:s + slice_P]
         if precision == "fp16":
@@ -62,11 +71,9 @@ def select_nearest(Qg, Vp, E, metric=METRIC_IP, precision="tf32", slice_P=8192):
         else:
             with reduced_precision(precision == "tf32"):
                 sc = Qg @ V.T
-        c = (1.0 - sc) if metric == METRIC_IP else ((V * V).sum(1).view(1, -1) - 2.0 * sc + qn)
-        v, i = torch.topk(c, min(E, c.shape[1]), dim=1, largest=False)
-        bv = torch.cat([bv, v], 1)
-        bi = torch.cat([bi, i + s], 1)
-        if bv.shape[1] > E:
-            v, j = torch.topk(bv, E, dim=1, largest=False)
-            bv, bi = v, torch.gather(bi, 1, j)
+        sc = sc.contiguous()
+        vn = (V * V).sum(1).contiguous() if metric != METRIC_IP else None
+        rc = N.lib().swb_select_topk(N.ptr(sc), n, V.shape[0], sc.stride(0), N.ptr(vn), N.ptr(qn), int(metric), Ee,
+                                     s, N.ptr(bd), N.ptr(bi), int(s > 0), stream)
+        N.check(rc, "swb_select_topk")
     return bi
