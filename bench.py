@@ -501,9 +501,18 @@ def run(args):
     peak, peak_kind = measured_peak_hbm()
     achieved = alg_bytes / (fused_ms / 1e3) / 1e9
     prof = profile_traffic(f"search_fused_{args.config}")
+    traffic, traffic_src = None, None
+    if prof:
+        same = prof.get("batch") == batch and prof.get("op") == [op["branches"], op["queue"], op["stop_eps"]]
+        if same:
+            traffic, traffic_src = prof["traffic_per_launch"], "ncu, this launch shape: " + prof["source"]
+        else:   # same kernel and corpus, another batch or operating point: scale by this run's bytes
+            traffic = round(prof["traffic_over_algorithmic"] * alg_bytes)
+            traffic_src = "ncu traffic/algorithmic ratio %.3f x this run's algorithmic bytes (%s)" % (
+                prof["traffic_over_algorithmic"], prof["source"])
     roofline = {"bound": "hbm", "kernel": "swb::fused_kernel", "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": prof.get("traffic_per_launch") if prof else None,
+                "traffic": traffic, "traffic_source": traffic_src,
                 "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": round(fused_ms, 3),
                 "prepare_ms": round(prep_ms, 3),
                 "per_query": {"distinct_nodes_scored": nodes / batch, "expansions": exps / batch}}
