@@ -59,7 +59,7 @@ CONFIGS = {
                 desc="C3-shaped profiling case: 200k x 1536 fp16 inner product, 200 clusters"),
 }
 LADDER = [(32, 12), (32, 16), (64, 16), (64, 24), (128, 32)]
-EPS = [0.0, 0.02, 0.05, 0.08, 0.12, 0.2, 0.3]
+EPS = [0.0, 0.01, 0.02, 0.05, 0.08, 0.12, 0.2, 0.3]   # the reference grid (reproduce.sh) plus 0
 TARGET = 0.95
 
 

@@ -362,18 +362,18 @@ __device__ __noinline__ RowState flush_rows(const Params& P, const float* bufd, 
 // The filter over 16 consecutive columns j0 .. j0+15 of this thread's row:
 // every value below the row's threshold goes to the row's buffer.  Ids already
 // merged into the row's best list are all below j0, so the (distance, id) key
-// order reduces to the distance alone here.  The 16 distances and the keep
-// mask are independent of one another; the stores happen only when some lane
-// of the warp keeps a value, each at cnt + (kept values before it), written in
-// column order so that a discarded value's store is overwritten by the next
-// kept one (positions stay below cnt + 16 <= BUF: a group starts at
-// cnt <= BUF - GROUP).  TAIL: only the first `lim` columns lie inside the
-// corpus.
+// order reduces to the distance alone here.  The common case -- nothing in the
+// group beats the threshold on any lane of the warp -- costs the 16 distances,
+// a balanced min tree and one vote.  Otherwise each kept value is stored at
+// cnt + (kept values before it), in column order, so a discarded value's store
+// is overwritten by the next kept one (positions stay below cnt + 16 <= BUF: a
+// group starts at cnt <= BUF - GROUP).  Returns whether any lane of the warp
+// kept a value (warp-uniform).  TAIL: only the first `lim` columns lie inside
+// the corpus.
 template <int METRIC, bool TAIL>
-__device__ __forceinline__ void filter16(const float* v, const float* nrm, float an, int j0, int lim, float th,
+__device__ __forceinline__ bool filter16(const float* v, const float* nrm, float an, int j0, int lim, float th,
                                          int& cnt, float* myd, int* myi) {
     float d[16];
-    unsigned lo = 0, hi = 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         if (METRIC == METRIC_IP) {
@@ -382,21 +382,26 @@ __device__ __forceinline__ void filter16(const float* v, const float* nrm, float
             float e = __fadd_rn(__fsub_rn(nrm[i], __fmul_rn(2.f, v[i])), an);
             d[i] = e < 0.f ? 0.f : e;
         }
-        bool p = d[i] < th;
-        if (TAIL) p = p && i < lim;
-        if (i < 8) lo |= (p ? 1u : 0u) << i;
-        else hi |= (p ? 1u : 0u) << (i - 8);
+        if (TAIL && i >= lim) d[i] = __int_as_float(0x7f800000);
     }
-    const unsigned m = lo | (hi << 8);
-    if (__any_sync(FULL, m != 0)) {
+    float m[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int pos = cnt + __popc(m & ((1u << i) - 1u));
-            myd[pos * BM] = d[i];
-            myi[pos * BM] = j0 + i;
-        }
-        cnt += __popc(m);
+    for (int i = 0; i < 8; ++i) m[i] = fminf(d[2 * i], d[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = fminf(m[2 * i], m[2 * i + 1]);
+    const float mn = fminf(fminf(m[0], m[1]), fminf(m[2], m[3]));
+    if (!__any_sync(FULL, mn < th)) return false;
+    unsigned mk = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) mk |= (d[i] < th ? 1u : 0u) << i;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int pos = cnt + __popc(mk & ((1u << i) - 1u));
+        myd[pos * BM] = d[i];
+        myi[pos * BM] = j0 + i;
     }
+    cnt += __popc(mk);
+    return true;
 }
 
 template <int MODE>
@@ -555,15 +560,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                     const int c0 = ch * 32 + g * GROUP;   // column within the tile
                     const float* nrm = norms_s + acc * BN + c0;
                     const int l = lim - c0;
+                    bool kept;
                     if (P.metric == METRIC_IP) {
-                        if (l >= GROUP) filter16<METRIC_IP, false>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
-                        else filter16<METRIC_IP, true>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
+                        kept = (l >= GROUP)
+                                   ? filter16<METRIC_IP, false>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi)
+                                   : filter16<METRIC_IP, true>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
                     } else {
-                        if (l >= GROUP) filter16<METRIC_L2, false>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
-                        else filter16<METRIC_L2, true>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
+                        kept = (l >= GROUP)
+                                   ? filter16<METRIC_L2, false>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi)
+                                   : filter16<METRIC_L2, true>(v + g * GROUP, nrm, an, cbase + c0, l, rs.th, rs.cnt, myd, myi);
                     }
-                    const bool full = rs.cnt > BUF - GROUP;
-                    if (__any_sync(FULL, full)) rs = flush_rows(P, bufd, bufi, lane, t, lrow, rb0, full, rs);
+                    if (kept) {   // warp-uniform: only a group that stored can fill a buffer
+                        const bool full = rs.cnt > BUF - GROUP;
+                        if (__any_sync(FULL, full)) rs = flush_rows(P, bufd, bufi, lane, t, lrow, rb0, full, rs);
+                    }
                 }
             }
         }
