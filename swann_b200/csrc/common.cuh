@@ -283,8 +283,20 @@ __device__ __forceinline__ float split_partial(const float* __restrict__ sq, con
 // tl issues the loads of up to SEG of its chunks (tl, tl + TEAM, ...) at once,
 // then sums them in order; wider rows take several such segments.
 #ifndef SWB_LDG_SEG
-#define SWB_LDG_SEG 6
+#define SWB_LDG_SEG 4
 #endif
+// One 16-byte chunk of a corpus row, read without allocating in L1: a row is
+// read once per query, and L1 is worth more to the spilled registers (2% on
+// the C3 search, measured; an L2 evict-first policy on top measured slower --
+// hub rows are re-read by other queries from L2).
+__device__ __forceinline__ uint4 ld_row16(const uint4* p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
 template <int TEAM, typename XT>
 __device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, const XT* __restrict__ grow,
                                                   int dim, int metric, int tl) {
@@ -298,7 +310,7 @@ __device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, 
 #pragma unroll
         for (int u = 0; u < SEG; ++u) {
             const int c = s0 + u * TEAM;
-            raw[u] = (c < nch) ? __ldg(r4 + c) : make_uint4(0u, 0u, 0u, 0u);
+            raw[u] = (c < nch) ? ld_row16(r4 + c) : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
         for (int u = 0; u < SEG; ++u) {

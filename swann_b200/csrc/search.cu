@@ -71,6 +71,18 @@ struct Knobs {
 
 __host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
 
+// A branch's NCTR counters (local_search.cu:35-41), spread over the warp: lane
+// c holds counter c; counter 0 (expansions) is also on every lane for the loop
+// tests.  Two registers instead of NCTR.
+struct Ctr {
+    int mine, exp;
+    __device__ void zero() { mine = 0; exp = 0; }
+    __device__ void add(int lane, int c, int v) { mine += (lane == c) ? v : 0; }
+    __device__ void set(int lane, int c, int v) { if (lane == c) mine = v; }
+    __device__ void expand() { ++exp; }
+    __device__ int value(int lane) const { return lane == 0 ? exp : mine; }
+};
+
 struct Layout {
     int q, ring, mbar, s_id, s_d, s_e, s_l, n_id, n_d, n_e, n_l, c_id, c_d, c_l, w_v, w_slot, w_d, w_aux,
         retired, total;
@@ -470,7 +482,7 @@ __device__ __forceinline__ void swap_queue(WarpMem& w) {
 // first occurrence (the CPU reference's rule, _refcpu.py:68-74).
 template <int TEAM, int TP, typename XT>
 __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring,
-                            int* ctr) {
+                            Ctr& ctr) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     if (vis) {
         if (K.H >= 128) {
@@ -480,7 +492,7 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
             for (int t = lane; t < K.H; t += 32) vis[t] = 0;
         }
     }
-    for (int c = 0; c < NCTR; ++c) ctr[c] = 0;
+    ctr.zero();
     const int V = K.V;
     int nsort = 2;
     while (nsort < V && nsort < MAXV) nsort <<= 1;
@@ -512,8 +524,8 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
     __syncwarp();
     if (K.loader) score_rows_ldg<TEAM, XT>(K, w, m, sq, nullptr, lane);
     else score_rows<TEAM, TP, XT>(K, w, m, ring, sq, nullptr, lane);
-    ctr[1] += m;
-    ctr[2] += fails;
+    ctr.add(lane, 1, m);
+    ctr.add(lane, 2, fails);
     for (int t = lane; t < m; t += 32) {
         const int si = w.w_aux[t];
         w.c_id[si] = w.w_v[t];
@@ -534,7 +546,7 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
 
 // The walk: up to `delta` expansions (local_search.cu:451-683).
 template <int TEAM, int TP, typename XT>
-__device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring, int* ctr,
+__device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring, Ctr& ctr,
                      int delta) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     uint64_t* ctab = (K.Hc > 0) ? K.cache + (size_t)q * (size_t)K.Hc : nullptr;
@@ -549,7 +561,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
     __syncwarp();
 
     for (int step = 0; step < delta; ++step) {
-        if (ctr[0] >= K.max_exp) break;
+        if (ctr.exp >= K.max_exp) break;
         float radius = (kr > 0 && w.s_id[kr - 1] >= 0) ? w.s_d[kr - 1] : FLT_MAX;
         if (bnd) {
             float gb = 0.f;
@@ -558,16 +570,16 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             if (gb < radius) radius = gb;
         }
         const float limit = (radius == FLT_MAX) ? FLT_MAX : __fmul_rn(radius, one_eps);
-        const int slot = select_slot(K, w, lane, ctr[0], limit, early);
+        const int slot = select_slot(K, w, lane, ctr.exp, limit, early);
         if (slot < 0) {
-            ctr[3] = 1;
+            ctr.set(lane, 3, 1);
             break;
         }
         const int p = w.s_id[slot];
         const int plin = w.s_l[slot];
         __syncwarp();
         if (lane == 0) w.s_e[slot] = 1;
-        ctr[0] += 1;
+        ctr.expand();
 
         // -- expand p: one lane per neighbour slot ------------------------
         int nv[4], nst[4], nsl[4];
@@ -634,57 +646,63 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
                 nd[t] = d;
             }
         }
-        // rows to score, compacted in slot order
-        int m = 0, pos[4], claimed_rows = 0;
+        // Candidates for the queue: what can still enter it (at most as far as
+        // its current worst; the queue does not change until the merge).  The
+        // ones with a known distance go to the candidate list now and the rows
+        // to score to the work list, so no per-neighbour register state lives
+        // across the scoring; the list is sorted by (distance, id) before the
+        // merge, so the order it is filled in does not matter.
+        const float worst = (w.s_id[L - 1] >= 0) ? w.s_d[L - 1] : FLT_MAX;
+        int m = 0, nk = 0, claimed_rows = 0;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
             const unsigned msk = __ballot_sync(FULL, nst[t] == 2);
-            pos[t] = m + __popc(msk & lanemask_lt());
             if (nst[t] == 2) {
-                w.w_v[pos[t]] = nv[t];
-                w.w_slot[pos[t]] = nsl[t];
+                const int ps = m + __popc(msk & lanemask_lt());
+                w.w_v[ps] = nv[t];
+                w.w_slot[ps] = nsl[t];
             }
             m += __popc(msk);
             claimed_rows += __popc(__ballot_sync(FULL, nst[t] == 2 && nsl[t] >= 0));
+            const bool keep = nst[t] == 1 && (worst == FLT_MAX || nd[t] <= worst);
+            const unsigned km = __ballot_sync(FULL, keep);
+            if (keep) {
+                const int ps = nk + __popc(km & lanemask_lt());
+                w.c_id[ps] = nv[t];
+                w.c_d[ps] = nd[t];
+                w.c_l[ps] = (uint8_t)plin;
+            }
+            nk += __popc(km);
         }
         __syncwarp();
         const bool scored = K.loader ? score_rows_ldg<TEAM, XT>(K, w, m, sq, ctab, lane)
                                      : score_rows<TEAM, TP, XT>(K, w, m, ring, sq, ctab, lane);
         if (!scored) break;
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-            if (nst[t] == 2) {
-                nd[t] = w.w_d[pos[t]];
-                nst[t] = 1;
+        for (int b = 0; b < m; b += 32) {
+            const int i = b + lane;
+            const float d = (i < m) ? w.w_d[i] : FLT_MAX;
+            const bool keep = i < m && (worst == FLT_MAX || d <= worst);
+            const unsigned km = __ballot_sync(FULL, keep);
+            if (keep) {
+                const int ps = nk + __popc(km & lanemask_lt());
+                w.c_id[ps] = w.w_v[i];
+                w.c_d[ps] = d;
+                w.c_l[ps] = (uint8_t)plin;
             }
+            nk += __popc(km);
+        }
         for (int off = 16; off > 0; off >>= 1) {
             cov += __shfl_xor_sync(FULL, cov, off);
             nbr += __shfl_xor_sync(FULL, nbr, off);
             fails += __shfl_xor_sync(FULL, fails, off);
             hits += __shfl_xor_sync(FULL, hits, off);
         }
-        ctr[1] += m;
-        ctr[2] += fails;
-        ctr[4] += hits;
-        ctr[5] += claimed_rows;
-
-        // -- keep what can still enter the queue, sort it, merge ------------
-        const float worst = (w.s_id[L - 1] >= 0) ? w.s_d[L - 1] : FLT_MAX;
-        int nk = 0;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const bool keep = nst[t] == 1 && (worst == FLT_MAX || nd[t] <= worst);
-            const unsigned msk = __ballot_sync(FULL, keep);
-            if (keep) {
-                const int ps = nk + __popc(msk & lanemask_lt());
-                w.c_id[ps] = nv[t];
-                w.c_d[ps] = nd[t];
-                w.c_l[ps] = (uint8_t)plin;
-            }
-            nk += __popc(msk);
-        }
-        ctr[8] += nk;
-        ctr[9] += 1;
+        ctr.add(lane, 1, m);
+        ctr.add(lane, 2, fails);
+        ctr.add(lane, 4, hits);
+        ctr.add(lane, 5, claimed_rows);
+        ctr.add(lane, 8, nk);
+        ctr.add(lane, 9, 1);
         __syncwarp();
         if (nk > 0) {
             if (nk <= 32) {
@@ -717,7 +735,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             if (cv >= K.crowd_frac) {
                 if (++crowd_run >= 2) {
                     set_retired(w, (unsigned)plin, lane);
-                    ctr[7] += 1;
+                    ctr.add(lane, 7, 1);
                     crowd_run = 0;
                 }
             } else {
@@ -729,7 +747,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             if (bk < best_k) { best_k = bk; stall = 0; }
             else stall += 1;
             if (stall >= K.stall_patience) {
-                ctr[6] = 1;
+                ctr.set(lane, 6, 1);
                 break;
             }
         }
@@ -755,7 +773,7 @@ __device__ __forceinline__ void load_query(float* sq, const float* src, int dim,
     for (int t = tid; t < dim / 4; t += nthreads) d4[t] = __ldg(&s4[t]);
 }
 
-__device__ void load_state(const Knobs& K, WarpMem& w, size_t bid, int lane, int* ctr) {
+__device__ void load_state(const Knobs& K, WarpMem& w, size_t bid, int lane, Ctr& ctr) {
     const size_t o = bid * (size_t)K.L;
     for (int i = lane; i < K.L; i += 32) {
         w.s_id[i] = K.ids[o + i];
@@ -763,11 +781,12 @@ __device__ void load_state(const Knobs& K, WarpMem& w, size_t bid, int lane, int
         w.s_e[i] = K.expd[o + i];
         w.s_l[i] = K.lin[o + i];
     }
-    for (int c = 0; c < NCTR; ++c) ctr[c] = K.counters[bid * NCTR + c];
+    ctr.mine = (lane < NCTR) ? K.counters[bid * NCTR + lane] : 0;
+    ctr.exp = __shfl_sync(FULL, ctr.mine, 0);
     __syncwarp();
 }
 
-__device__ void store_state(const Knobs& K, const WarpMem& w, size_t bid, int lane, const int* ctr) {
+__device__ void store_state(const Knobs& K, const WarpMem& w, size_t bid, int lane, const Ctr& ctr) {
     if (K.ids) {
         const size_t o = bid * (size_t)K.L;
         for (int i = lane; i < K.L; i += 32) {
@@ -777,13 +796,7 @@ __device__ void store_state(const Knobs& K, const WarpMem& w, size_t bid, int la
             K.lin[o + i] = w.s_l[i];
         }
     }
-    if (K.counters && lane < NCTR) {
-        int v = ctr[0];
-#pragma unroll
-        for (int c = 1; c < NCTR; ++c)
-            if (lane == c) v = ctr[c];
-        K.counters[bid * NCTR + lane] = v;
-    }
+    if (K.counters && lane < NCTR) K.counters[bid * NCTR + lane] = ctr.value(lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -811,7 +824,7 @@ __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs
     }
     if (K.bound && j == 0 && lane == 0) K.bound[q] = FLT_MAX;
     __syncwarp();
-    int ctr[NCTR];
+    Ctr ctr;
     init_branch<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr);
     store_state(K, w, (size_t)q * K.J + j, lane, ctr);
 }
@@ -835,7 +848,7 @@ __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Kn
     Ring ring;
     ring_setup(K, w, lane, ring);
     load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
-    int ctr[NCTR];
+    Ctr ctr;
     load_state(K, w, (size_t)flat, lane, ctr);
     walk<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
     __syncwarp();
@@ -883,8 +896,13 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
     for (int t = w + lane; t < k; t += 32) { oi[t] = -1; od[t] = __int_as_float(0x7f800000); }
 }
 
+// Register budget of the fused kernel: 65536 / (256 * 5) -> 48 registers a
+// thread, with 4 warps (4 branches) a CTA.  Measured at C3 (1M x 1536 fp16,
+// batch 65535): occupancy buys more than the spills it costs -- 48 registers
+// and 4-chunk segments ran 4% faster than 64 registers and 6-chunk segments,
+// and 80 registers (no spills) ran slowest.
 #ifndef SWB_FUSED_MINB
-#define SWB_FUSED_MINB 4
+#define SWB_FUSED_MINB 5
 #endif
 template <int TEAM, int TP, typename XT>
 __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
@@ -901,7 +919,7 @@ __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid
     WarpMem w = carve(smem + qbytes + (size_t)warp * K.warp_bytes, lay);
     Ring ring;
     ring_setup(K, w, lane, ring);
-    int ctr[NCTR];
+    Ctr ctr;
     init_branch<TEAM, TP, XT>(K, w, q, j, lane, sq, ring, ctr);
     walk<TEAM, TP, XT>(K, w, q, j, lane, sq, ring, ctr, K.max_exp);
     __syncwarp();
@@ -1207,7 +1225,7 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.status = status; K.k = k; K.kk = k < L ? k : L;
     K.branch_ids = branch_ids; K.branch_dist = branch_dist; K.qdone = qdone;
     K.out_ids = out_ids; K.out_dist = out_dist;
-    int W = abi::env_int("SWB_WARPS", 2);
+    int W = abi::env_int("SWB_WARPS", 4);
     if (W > J) W = J;
     if (W < 1) W = 1;
     if (W > 8) W = 8;
