@@ -30,6 +30,8 @@ MAX_BATCH = 65535
 # Bytes of per-query distance tables one launch may use; larger batches are
 # searched in consecutive chunks on the same stream.
 TABLE_BUDGET = 24 << 30
+# host batches larger than this are copied in chunks that overlap the search
+COPY_CHUNK = 8192
 
 
 @dataclass
@@ -142,18 +144,30 @@ class Index:
             if b <= a:
                 continue
             with torch.cuda.device(r.dev):
-                if host is not None:
-                    Qd = host[a:b].to(r.dev, non_blocking=True)
-                else:
-                    Qd = queries[a:b].to(r.dev, non_blocking=True)
-                Qd = Qd.float().contiguous()
-                ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
-                seeds = r.catalogue[ent].to(torch.int32)
                 Hc = self.table_slots or E.cache_size(cfg.branches, cfg.budget, r.G.shape[1])
-                step = max(1, min(Qd.shape[0], TABLE_BUDGET // (8 * Hc)))
-                for c0 in range(0, Qd.shape[0], step):
-                    c1 = min(Qd.shape[0], c0 + step)
-                    outs.append(_search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc))
+                if host is not None and b - a > COPY_CHUNK:
+                    # Host queries: copied chunk by chunk on a side stream, each
+                    # chunk searched while the next one is in flight (the copy
+                    # overlaps the search when the host memory is pinned).
+                    comp = torch.cuda.current_stream(r.dev)
+                    side = self._copy_stream(r.dev)
+                    buf = torch.empty((b - a, host.shape[1]), dtype=host.dtype, device=r.dev)
+                    side.wait_stream(comp)   # buf's memory is ready on the search stream
+                    ready = []
+                    with torch.cuda.stream(side):
+                        for c0 in range(0, b - a, COPY_CHUNK):
+                            c1 = min(b - a, c0 + COPY_CHUNK)
+                            buf[c0:c1].copy_(host[a + c0:a + c1], non_blocking=True)
+                            ev = torch.cuda.Event()
+                            ev.record(side)
+                            ready.append((c0, c1, ev))
+                    for c0, c1, ev in ready:
+                        comp.wait_event(ev)
+                        self._search_part(r, buf[c0:c1].float().contiguous(), k, cfg, Hc, outs)
+                else:
+                    src = host if host is not None else queries
+                    Qd = src[a:b].to(r.dev, non_blocking=True).float().contiguous()
+                    self._search_part(r, Qd, k, cfg, Hc, outs)
         if E._OVERFLOW_GUARD:
             for _, _, ctr, status in outs:
                 if ctr is not None and int(ctr[..., 2].sum()) != 0:
@@ -164,6 +178,23 @@ class Index:
         ids = torch.cat([o[0].to(dev0) for o in outs]) if outs else torch.empty((0, k), dtype=torch.int32)
         dist = torch.cat([o[1].to(dev0) for o in outs]) if outs else torch.empty((0, k))
         return ids, dist
+
+    def _search_part(self, r, Qd, k, cfg, Hc, outs):
+        """Seed selection and the fused search of one device-resident block of
+        queries, in table-budget sized launches."""
+        ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
+        seeds = r.catalogue[ent].to(torch.int32)
+        step = max(1, min(Qd.shape[0], TABLE_BUDGET // (8 * Hc)))
+        for c0 in range(0, Qd.shape[0], step):
+            c1 = min(Qd.shape[0], c0 + step)
+            outs.append(_search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc))
+
+    def _copy_stream(self, dev):
+        streams = self.__dict__.setdefault("_copy_streams", {})
+        key = torch.device(dev).index
+        if key not in streams:
+            streams[key] = torch.cuda.Stream(device=dev)
+        return streams[key]
 
     # -- persistence -----------------------------------------------------
     def save(self, path) -> None:

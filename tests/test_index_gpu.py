@@ -112,3 +112,26 @@ def test_replicas_shard_queries(ip_index):
 def test_overflow_guard_round_trip():
     was = swann.overflow_guard(False)
     assert swann.overflow_guard(was) is False
+
+
+def test_host_batches_larger_than_a_copy_chunk(ip_index):
+    """Host queries beyond one copy chunk are copied and searched chunk by chunk
+    (copies overlapping the search); the answers match the device path's."""
+    from swann_b200 import index as I
+    X, _, idx = ip_index
+    nq = 2 * I.COPY_CHUNK + 123
+    rng = np.random.default_rng(9)
+    Q = rng.standard_normal((nq, X.shape[1]), dtype=np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    pinned = torch.from_numpy(Q).pin_memory()
+    for src in (Q, pinned):
+        ids, dist = idx.search(src, k=10)
+        assert ids.shape == (nq, 10) and dist.shape == (nq, 10)
+        assert (ids >= 0).all()
+        sample = np.arange(0, nq, 97)
+        for q in sample:
+            assert len(set(ids[q])) == 10
+            assert np.allclose(dist[q], 1.0 - X[ids[q]].astype(np.float64) @ Q[q].astype(np.float64), atol=1e-5)
+        dev_ids, _ = idx.search(torch.from_numpy(Q).cuda(), k=10)
+        truth = exact(X, Q[sample], 10, "ip")
+        assert abs(recall(ids[sample], truth, 10) - recall(dev_ids[sample], truth, 10)) < 0.01
