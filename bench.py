@@ -613,7 +613,18 @@ def run_reference(args):
     X, G, _ = build_index(cfg, dev, 1, 0)
     index = swann.Index(X, G, metric=cfg["metric"])
     Q = make_queries(cfg, dev, 0, cfg["batch"])
-    op = dict(branches=32, queue=12, stop_eps=0.05)
+    # the operating point of the other arm: --fixed, or the same calibration
+    # (recall >= TARGET on the ground-truth subset; untimed setup, like the build)
+    if args.fixed:
+        b, q, e = args.fixed.split(",")
+        op = dict(branches=int(b), queue=int(q), stop_eps=float(e))
+    else:
+        gt_n = min(cfg["batch"], args.gt)
+        truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
+        best, tried = calibrate(index, Q[:gt_n], truth, cfg)
+        if best is None:
+            best = max(tried, key=lambda t: t[3])
+        op = dict(branches=best[0], queue=best[1], stop_eps=best[2])
     from swann_b200 import _select as S
     ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
     seeds = index.catalogue[ent].to(torch.int32)
@@ -641,9 +652,80 @@ def run_reference(args):
             "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], **op, "budget": 64, "team": 16},
             "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": cores, "kind": "port",
                              "sample": f"{per} queries per step (C restatement of swann/_refcpu.py, independent "
-                                       f"branches, {cores} threads); index built on the GPU beforehand"},
+                                       f"branches, {cores} threads); index built and the operating point "
+                                       f"calibrated on the GPU beforehand, untimed"},
             "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# C3's batch schedule: branches 128 up to batch 64, 64 at
+# 512, 32 from 4096 on
+BATCH_SWEEP = [(1, 128), (8, 128), (64, 128), (512, 64), (4096, 32), (65535, 32)]
+
+
+def run_batch_sweep(args):
+    """QPS and per-batch latency across batch sizes on one GPU, one index.
+    The operating point per branch count is the smallest stop_eps (queue 12)
+    reaching recall@10 >= TARGET on the ground-truth subset (recall does not
+    depend on the batch: queries are independent); each batch size is then
+    timed over consecutive slices of the query set with CUDA events."""
+    dist_setup()
+    dev = torch.device("cuda", 0)
+    cfg = dict(CONFIGS[args.config])
+    import swann_b200 as swann
+    X, G, _ = build_index(cfg, dev, 1, 0)
+    torch.cuda.empty_cache()
+    index = swann.Index(X, G, metric=cfg["metric"])
+    nmax = max(b for b, _ in BATCH_SWEEP)
+    Q = make_queries(cfg, dev, 0, nmax)
+    gt_n = min(nmax, args.gt)
+    truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
+    from swann_b200 import _engine as E
+    from swann_b200 import _select as S
+    ops = {}
+    for _, br in BATCH_SWEEP:
+        if br in ops:
+            continue
+        index.table_slots = None
+        for eps in EPS:
+            ids, _ = index.search_tensors(Q[:gt_n], k=cfg["k"], branches=br, queue=12, stop_eps=eps)
+            r = recall(ids.cpu().numpy(), truth, cfg["k"])
+            if r >= TARGET:
+                break
+        # table sized from measured claims, as the main line does
+        sd = index.catalogue[S.select_nearest(Q[:gt_n], index._cat, br, metric=index._m)].to(torch.int32)
+        _, _, ctr, _ = E.search_fused_lean(X, G, Q[:gt_n], sd, k=cfg["k"], L=12, B=64, metric=index._m,
+                                           team_size=16, stop_eps=eps, shared_cache=True, shared_bound=True,
+                                           exclusive=2, elide_visited=True)
+        claims = (ctr[..., 5].to(torch.int64).sum(1) + br).max().item()
+        ops[br] = (eps, r, min(E.cache_size(br, 64, G.shape[1]), max(4096, E.next_pow2(2 * int(claims)))))
+    rows = []
+    for b, br in BATCH_SWEEP:
+        eps, r, slots = ops[br]
+        index.table_slots = slots
+        kw = dict(k=cfg["k"], branches=br, queue=12, stop_eps=eps)
+        reps = max(args.steps, min(200, nmax // b))
+        for i in range(args.warmup):
+            index.search_tensors(Q[(i * b) % (nmax - b + 1):][:b], **kw)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            a = (i * b) % (nmax - b + 1)
+            index.search_tensors(Q[a:a + b], **kw)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        rows.append({"batch": b, "branches": br, "queue": 12, "stop_eps": eps, "recall@10": round(r, 4),
+                     "table_slots": slots,
+                     "ms_per_batch": round(ms, 3), "qps": round(b / (ms / 1e3), 1), "batches_timed": reps})
+    line = {"metric": f"QPS and latency by batch size at recall@10>={TARGET} ({cfg['desc']})",
+            "unit": "queries/s", "n_gpus": 1, "higher_is_better": True, "dtype": "f32",
+            "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
+            "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], "k": cfg["k"], "budget": 64,
+                       "team": 16, "recall_sample": gt_n, "timing": "CUDA events, device-resident queries"},
+            "batches": rows}
     print(json.dumps(line), flush=True)
 
 
@@ -659,11 +741,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--fixed", default="", help="branches,queue,stop_eps: skip the calibration")
     ap.add_argument("--build-only", action="store_true", help="time the graph build instead of the search")
+    ap.add_argument("--batch-sweep", action="store_true", help="QPS and latency across the C3 batch sizes")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.build_only:
         run_build(args)
+    elif args.batch_sweep:
+        run_batch_sweep(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
