@@ -82,6 +82,13 @@ SWB_API int swb_search_init(const void* X, int x_dtype, int64_t n, int dim,
  * `active`) by up to `delta` expansions, in place; resumable: advance(a) then
  * advance(b) equals advance(a + b).
  *   G        [n, D] int32 adjacency, -1 = no edge, D <= SWB_MAX_DEGREE
+ *   codes    optional sign-code prefilter (local_search.cu:205-243,560-572;
+ *            the reference's advance(..., codes, alpha, cmu, margin)), inner
+ *            product only: codes [n, code_words] int32, bit i set when
+ *            x_i > mu_i, code_words = ceil(dim / 32); code_alpha [n] the
+ *            per-node scale |x - mu|_1 / dim; code_mu [dim] the corpus mean.
+ *            A neighbour whose estimated distance exceeds the step's expansion
+ *            limit by more than code_margin is not read.  NULL = off.
  *   status   optional int32 device word; a device-side wait that runs out sets
  *            it to SWB_ERR_TIMEOUT (never set in normal operation) */
 SWB_API int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim,
@@ -94,6 +101,8 @@ SWB_API int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim,
                        uint64_t* cache, int Hc, float* bound, int exclusive,
                        int stall_patience, float crowd_frac,
                        const int32_t* active, int n_active,
+                       const int32_t* codes, const float* code_alpha, const float* code_mu,
+                       float code_margin, int code_words,
                        int32_t* status, void* stream);
 
 /* Replaces merge_branches (swann/csrc/local_search.cu:925-947, and the tensor

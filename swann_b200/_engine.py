@@ -19,6 +19,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib as N
@@ -254,8 +255,9 @@ def advance(X, G, Qv, state: SearchState, delta_expansions: int, active=None, co
     _check_inputs(X, Qv)
     if not (G.is_cuda and G.dtype == torch.int32 and G.is_contiguous()):
         raise ValueError("G: contiguous cuda int32")
+    code_args = (None, None, None, 0.0, 0)
     if codes is not None:
-        raise NotImplementedError("the sign-code prefilter is not part of this build")
+        code_args = _code_args(codes, X, state)
     Q, J, L = state.ids.shape
     H = state.visited.shape[2]
     Hc = state.cache.shape[1] if state.cache is not None and state.cache.numel() else 0
@@ -273,13 +275,44 @@ def advance(X, G, Qv, state: SearchState, delta_expansions: int, active=None, co
             int(delta_expansions), int(state.B), int(state.policy), int(state.V), float(state.stop_eps),
             int(state.kstop), N.ptr(state.cache), Hc, N.ptr(state.bound), int(state.exclusive),
             int(state.stall_patience), float(state.crowd_frac), N.ptr(active), n_active,
-            N.ptr(state.status), N.stream_of(X))
+            *code_args, N.ptr(state.status), N.stream_of(X))
     N.check(rc, "advance")
     return state
 
 
+def _code_args(codes, X, state):
+    """(codes, alpha, mu, margin) as load_codes returns them -> the ABI's five
+    code arguments, checked (swann/csrc/local_search.cu:778-841 takes them as
+    codes, alpha, cmu, margin)."""
+    if state.metric != METRIC_IP:
+        raise NotImplementedError("the sign-code prefilter is inner product only (local_search.cu:222-243)")
+    cd, al, mu, margin = codes
+    n, d = X.shape
+    words = (d + 31) // 32
+    cd = cd.to(device=X.device, dtype=torch.int32).contiguous()
+    al = al.to(device=X.device, dtype=torch.float32).contiguous()
+    mu = mu.to(device=X.device, dtype=torch.float32).contiguous()
+    if tuple(cd.shape) != (n, words) or tuple(al.shape) != (n,) or tuple(mu.shape) != (d,):
+        raise ValueError(f"codes must be [n, {words}] int32 with alpha [n] and mu [d]")
+    return (N.ptr(cd), N.ptr(al), N.ptr(mu), float(margin), words)
+
+
 def load_codes(data, name=None, margin=0.20, device="cuda"):
-    raise NotImplementedError("the sign-code prefilter is not part of this build")
+    """The sign code, its per-node scale and the corpus mean, as `advance` wants
+    (swann/_engine.py:320-337): codes_<name>.npy, alpha_<name>.npy and
+    mu_<name>.npy in a corpus directory, `name` from its manifest when not
+    given.  `margin` is in the corpus's distance units and is set per corpus.
+    `swann_b200.corpus.write_codes` writes these files."""
+    import json
+    from pathlib import Path
+    d = Path(data)
+    if name is None:
+        man = json.loads((d / "manifest.json").read_text())
+        name = "1bit" if man["metric"].startswith("ip") else "int8"
+    cd = torch.from_numpy(np.load(d / f"codes_{name}.npy")).to(device)
+    al = torch.from_numpy(np.load(d / f"alpha_{name}.npy")).to(device)
+    cm = torch.from_numpy(np.load(d / f"mu_{name}.npy")).to(device)
+    return cd.contiguous(), al.contiguous(), cm.contiguous(), margin
 
 
 def branch_topk(state: SearchState, k: int):

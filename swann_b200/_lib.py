@@ -29,7 +29,7 @@ SIGNATURES = {
                                   _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                                   _vp, _i32, _vp, _i32, _i32, _i32, _i32,
                                   _i32, _i32, _f32, _i32, _vp, _i32, _vp, _i32,
-                                  _i32, _f32, _vp, _i32, _vp, _vp]),
+                                  _i32, _f32, _vp, _i32, _vp, _vp, _vp, _f32, _i32, _vp, _vp]),
     "swb_merge_branches": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     "swb_search_prepare": (_i32, [_i32, _vp, _i32, _vp, _vp, _vp]),
     "swb_select_topk": (_i32, [_vp, _i64, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _vp]),

@@ -67,6 +67,13 @@ struct Knobs {
     float* out_dist;
     int W, R, warp_bytes, q_shared, cmax;
     int loader;   // 0: bulk copies into a shared-memory ring; 1: direct loads
+    // sign-code prefilter (advance only; null = off): codes [n][cwords] bits
+    // around the corpus mean cmu [dim], per-node scale calpha [n], margin
+    const int32_t* codes;
+    const float* calpha;
+    const float* cmu;
+    float cmargin;
+    int cwords;
 };
 
 __host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
@@ -545,7 +552,87 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
 }
 
 // The walk: up to `delta` expansions (local_search.cu:451-683).
-template <int TEAM, int TP, typename XT>
+// -- sign-code prefilter (local_search.cu:205-243, 560-572) ---------------
+//
+// <q, x> ~= alpha_x * <q, b_x> + <q, mu> with b_x in {-1, +1}^d the signs of
+// x - mu, so <q, b> = 2 * (sum of q over set bits) - sum(q).  The query's two
+// sums are taken once, in a fixed order (the reference adds them with float
+// atomics, whose order varies).
+__device__ __forceinline__ void code_query_sums(const float* sq, const float* cmu, int dim, int lane, float& qmu,
+                                                float& qsum) {
+    float a = 0.f, b = 0.f;
+    for (int i = lane; i < dim; i += 32) {
+        a = __fadd_rn(a, __fmul_rn(sq[i], cmu[i]));
+        b = __fadd_rn(b, sq[i]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        a = __fadd_rn(a, __shfl_xor_sync(FULL, a, off));
+        b = __fadd_rn(b, __shfl_xor_sync(FULL, b, off));
+    }
+    qmu = a;
+    qsum = b;
+}
+
+// The estimated distance 1 - <q, x> of row v, on every lane of its team.
+template <int TEAM>
+__device__ __forceinline__ float code_estimate(const Knobs& K, const float* sq, int v, float qmu, float qsum,
+                                               int tl) {
+    const uint32_t* code = reinterpret_cast<const uint32_t*>(K.codes) + (size_t)v * K.cwords;
+    float acc = 0.f;
+    for (int w = tl; w < K.cwords; w += TEAM) {
+        const uint32_t bits = __ldg(code + w);
+        const int base = w * 32;
+#pragma unroll 8
+        for (int b = 0; b < 32; ++b) {
+            const int i = base + b;
+            if (i < K.dim && (bits >> b) & 1u) acc = __fadd_rn(acc, sq[i]);
+        }
+    }
+#pragma unroll
+    for (int off = TEAM / 2; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, off, TEAM));
+    const float ip = __fadd_rn(__fmul_rn(__ldg(K.calpha + v), __fsub_rn(__fmul_rn(2.f, acc), qsum)), qmu);
+    return __fsub_rn(1.f, ip);
+}
+
+// Drops from the work list w_v/w_slot[0..m) every row whose estimate lies
+// beyond `limit` by more than the margin; its vector is never read and its
+// claimed table slot stays unscored.  Returns the rows kept; `skipped` gets
+// the count (on every lane).
+template <int TEAM>
+__device__ int code_filter(const Knobs& K, const WarpMem& w, int m, const float* sq, float limit, float qmu,
+                           float qsum, int lane, int& skipped) {
+    constexpr int P = 32 / TEAM;
+    const int team = lane / TEAM, tl = lane % TEAM;
+    for (int base = 0; base < m; base += P) {
+        const int i = base + team;
+        const int v = (i < m) ? w.w_v[i] : 0;
+        const float est = code_estimate<TEAM>(K, sq, v, qmu, qsum, tl);
+        if (tl == 0 && i < m) w.w_aux[i] = (est > __fadd_rn(limit, K.cmargin)) ? 1 : 0;
+    }
+    __syncwarp();
+    int kept = 0;
+    for (int b = 0; b < m; b += 32) {
+        const int i = b + lane;
+        const bool keep = i < m && w.w_aux[i] == 0;
+        const int v = keep ? w.w_v[i] : 0, sl = keep ? w.w_slot[i] : 0;
+        const unsigned km = __ballot_sync(FULL, keep);
+        __syncwarp();
+        if (keep) {
+            const int ps = kept + __popc(km & lanemask_lt());
+            w.w_v[ps] = v;
+            w.w_slot[ps] = sl;
+        }
+        kept += __popc(km);
+        __syncwarp();
+    }
+    skipped = m - kept;
+    return kept;
+}
+
+// CODES: compiled with the sign-code prefilter (the advance kernel, when
+// codes are given); the fused search never uses it.
+template <int TEAM, int TP, typename XT, bool CODES = false>
 __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring, Ctr& ctr,
                      int delta) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
@@ -558,6 +645,8 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
     float best_k = FLT_MAX;
     int stall = 0, crowd_run = 0;
     if (lane < 8) w.retired[lane] = 0u;
+    float qmu = 0.f, qsum = 0.f;
+    if (CODES) code_query_sums(sq, K.cmu, K.dim, lane, qmu, qsum);
     __syncwarp();
 
     for (int step = 0; step < delta; ++step) {
@@ -675,6 +764,13 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             nk += __popc(km);
         }
         __syncwarp();
+        if (CODES && limit != FLT_MAX && m > 0) {
+            int skipped = 0;
+            m = code_filter<TEAM>(K, w, m, sq, limit, qmu, qsum, lane, skipped);
+            claimed_rows = 0;   // recounted below from the rows actually scored
+            for (int b = 0; b < m; b += 32)
+                claimed_rows += __popc(__ballot_sync(FULL, b + lane < m && w.w_slot[b + lane] >= 0));
+        }
         const bool scored = K.loader ? score_rows_ldg<TEAM, XT>(K, w, m, sq, ctab, lane)
                                      : score_rows<TEAM, TP, XT>(K, w, m, ring, sq, ctab, lane);
         if (!scored) break;
@@ -850,7 +946,10 @@ __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Kn
     load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
     Ctr ctr;
     load_state(K, w, (size_t)flat, lane, ctr);
-    walk<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
+    if (K.codes)
+        walk<TEAM, TP, XT, true>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
+    else
+        walk<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
     __syncwarp();
     store_state(K, w, (size_t)flat, lane, ctr);
 }
@@ -1105,6 +1204,7 @@ int fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int te
     K.L = L;
     const int tp = pick_tp(K.rowbytes, team);
     K.loader = abi::env_int("SWB_LOADER", 1) ? 1 : 0;
+    K.codes = nullptr; K.calpha = nullptr; K.cmu = nullptr; K.cmargin = 0.f; K.cwords = 0;
     K.R = K.loader ? 0 : pick_ring(K.rowbytes, tp);
     K.q_shared = q_shared ? 1 : 0;
     int cm = pow2_at_least(D > V ? D : V);
@@ -1152,11 +1252,17 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
                                   int team, int delta, int max_expansions, int policy, int V, float stop_eps,
                                   int kstop, uint64_t* cache, int Hc, float* bound, int exclusive,
                                   int stall_patience, float crowd_frac, const int32_t* active, int n_active,
-                                  int32_t* status, void* stream) {
+                                  const int32_t* codes, const float* code_alpha, const float* code_mu,
+                                  float code_margin, int code_words, int32_t* status, void* stream) {
     int rc = common_checks(X, x_dtype, n, dim, team, L);
     if (rc) return rc;
     if (!G || D < 1 || D > MAXD) return abi::fail(SWB_ERR_ARG, "graph degree must be 1..%d", MAXD);
     if (V > 256) return abi::fail(SWB_ERR_ARG, "lineage count exceeds 256 (lineage is a uint8)");
+    if (codes) {
+        if (!code_alpha || !code_mu) return abi::fail(SWB_ERR_ARG, "codes need their scales and the corpus mean");
+        if (metric != SWB_METRIC_IP) return abi::fail(SWB_ERR_ARG, "the sign-code prefilter is inner product only");
+        if (code_words != (dim + 31) / 32) return abi::fail(SWB_ERR_ARG, "codes must have ceil(dim / 32) words a row");
+    }
     if (!pow2(H)) return abi::fail(SWB_ERR_ARG, "visited table size must be a power of two");
     if (Hc > 0 && !pow2(Hc)) return abi::fail(SWB_ERR_ARG, "cache size must be a power of two");
     if (Q <= 0 || J <= 0 || delta <= 0) return SWB_OK;
@@ -1171,6 +1277,8 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     K.exclusive = Hc > 0 ? exclusive : 0;
     K.stall_patience = stall_patience; K.crowd_frac = crowd_frac;
     K.active = active; K.n_active = active ? n_active : 0; K.status = status;
+    K.codes = codes; K.calpha = code_alpha; K.cmu = code_mu; K.cmargin = code_margin;
+    K.cwords = codes ? code_words : 0;
     K.W = 4;
     const long long warps = active ? (long long)n_active : (long long)Q * J;
     dim3 grid((unsigned)((warps + K.W - 1) / K.W));

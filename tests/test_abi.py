@@ -48,7 +48,7 @@ def test_argument_errors_need_no_gpu():
     L = N.lib()
     rc = L.swb_search_advance(1 << 20, 0, 10, 8, 1 << 20, 4, 1 << 20, 1 << 20, 1 << 20, 1 << 20, 1 << 20,
                               1, 1, 8, 1 << 20, 1, 1 << 20, 0, 12, 1, 1, 0, 1, -1.0, 10, None, 0, None, 0,
-                              0, 0.0, None, 0, None, None)
+                              0, 0.0, None, 0, None, None, None, 0.0, 0, None, None)
     assert rc == N.ERR_TEAM
     assert b"team" in L.swb_last_error()
     rc = L.swb_search_init(1 << 20, 0, 10, 8, 1 << 20, 1 << 20, 70000, 1, 1, 1 << 20, 1 << 20, 1 << 20, 1 << 20, 8,
