@@ -121,6 +121,78 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// -- a CTA pair (cluster of 2) sharing one M = 256 MMA ------------------------
+//
+// The leader (rank 0) issues tcgen05.mma.cta_group::2: A's 256 rows come 128
+// from each CTA's shared memory, B's N columns N/2 from each, and each CTA's
+// TMEM receives its own 128 rows x N.  Both CTAs load their halves with TMA
+// into their own shared memory and complete the transaction on the leader's
+// barrier; the leader's commits arrive on the matching barrier of both CTAs.
+// Every TMA load reads this GPU's memory into its own CTA only.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of this CTA's `p` in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    return a;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cbar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// TMA tile into this CTA's shared memory, completing on a barrier that may be
+// the leader's (cbar: a shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1, uint32_t cbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cbar)
+        : "memory");
+}
+template <int MODE>
+__device__ __forceinline__ void umma_pair(uint32_t dtm, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    if constexpr (MODE == MODE_F16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtm),
+            "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtm),
+            "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+            : "memory");
+    }
+}
+// completion of this CTA pair's MMAs so far, to the barrier at the same
+// shared-memory offset in both CTAs (a commit, not a load)
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+}
+
 // barrier of the 128 epilogue threads (named barrier 1) that also ANDs a
 // predicate across them, so every epilogue warp takes the same branch
 __device__ __forceinline__ bool epi_all(bool ok) {
@@ -157,23 +229,26 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p) {
     return ((a >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 
-template <int MODE>
+template <int MODE, bool PAIR>
 __host__ __device__ constexpr uint32_t instr_desc() {
     return (1u << 4)                                   // D in fp32
            | (Cfg<MODE>::FMT << 7) | (Cfg<MODE>::FMT << 10)   // A, B format
            | (uint32_t(Cfg<MODE>::BN >> 3) << 17)        // N
-           | (uint32_t(BM >> 4) << 24);                  // M
+           | (uint32_t((PAIR ? 2 * BM : BM) >> 4) << 24);   // M: 256 across a CTA pair
 }
 
 // -- shared memory ---------------------------------------------------------
 
-template <int MODE>
+// PAIR: a CTA holds half of each B tile, so a stage is smaller and the ring
+// deeper in the same shared memory
+template <int MODE, bool PAIR>
 struct Layout {
     static constexpr int BN = Cfg<MODE>::BN;
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
     static constexpr int A_BYTES = BM * ROW_BYTES;
-    static constexpr int B_BYTES = BN * ROW_BYTES;
+    static constexpr int B_BYTES = B_ROWS * ROW_BYTES;
     static constexpr int STAGE = Cfg<MODE>::NOPS * (A_BYTES + B_BYTES);
-    static constexpr int STAGES = Cfg<MODE>::STAGES;
+    static constexpr int STAGES = PAIR ? (MODE == MODE_F16 ? 6 : 4) : Cfg<MODE>::STAGES;
     static constexpr int RING = STAGES * STAGE;
     static constexpr int NORMS = RING;                          // float [2][BN]
     static constexpr int BUFD = NORMS + 2 * BN * 4;             // float [BUF][BM]
@@ -404,27 +479,22 @@ __device__ __forceinline__ bool filter16(const float* v, const float* nrm, float
     return true;
 }
 
-template <int MODE>
+// One CTA (PAIR = false), or one CTA of a pair (PAIR = true: launched as
+// clusters of two, the leader issuing M = 256 MMAs over both CTAs' tiles).
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constant__ CUtensorMap tmA,
                                                             const __grid_constant__ CUtensorMap tmA2,
                                                             const __grid_constant__ CUtensorMap tmB,
                                                             const __grid_constant__ CUtensorMap tmB2,
                                                             const __grid_constant__ Params P) {
-    using Ly = Layout<MODE>;
+    using Ly = Layout<MODE, PAIR>;
     constexpr int BN = Cfg<MODE>::BN;
-    constexpr int STAGES = Cfg<MODE>::STAGES;
+    constexpr int STAGES = Ly::STAGES;
     constexpr int KSUB = Cfg<MODE>::KSUB;
     constexpr int KELEM = (MODE == MODE_F16) ? 64 : 32;          // K elements per stage
-    constexpr uint32_t IDESC = instr_desc<MODE>();
+    constexpr uint32_t IDESC = instr_desc<MODE, PAIR>();
     extern __shared__ __align__(1024) char smem_raw[];
     char* sm = smem_raw;
-    // the 128B swizzle needs every stage on a 1024-byte boundary; the extern
-    // declaration asks for it, and a block that did not get it stops here
-    // (uniformly, before any barrier or TMEM allocation) with an error status
-    if (smem_u32(sm) & 1023u) {
-        if (threadIdx.x == 0 && P.status) atomicExch(P.status, SWB_ERR_SMEM);
-        return;
-    }
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ly::BARS);
     uint64_t* empty = full + STAGES;
     uint64_t* accf = empty + STAGES;
@@ -433,38 +503,48 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
     float* norms_s = reinterpret_cast<float*>(sm + Ly::NORMS);
     float* bufd = reinterpret_cast<float*>(sm + Ly::BUFD);
     int* bufi = reinterpret_cast<int*>(sm + Ly::BUFI);
+    __shared__ int s_abort_store;
+    volatile int* s_abort = &s_abort_store;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const bool leader = rank == 0;
     const int64_t rb0 = P.row0 + (int64_t)blockIdx.x * BM;   // first global row of this block
     const int ntiles = (int)((P.n + BN - 1) / BN);
     const int ksteps = P.dim / KELEM;
 
     if (threadIdx.x == 0) {
+        // the 128B swizzle needs every stage on a 1024-byte boundary; the extern
+        // declaration asks for it, and a block that did not get it does no work
+        // (it still takes part in every barrier, so a pair cannot hang on it)
+        *s_abort = (smem_u32(sm) & 1023u) ? 2 : 0;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(&accf[0], 1);
         mbar_init(&accf[1], 1);
-        mbar_init(&acce[0], 128);
-        mbar_init(&acce[1], 128);
+        mbar_init(&acce[0], PAIR ? 256 : 128);   // a pair's leader hears both CTAs' epilogues
+        mbar_init(&acce[1], PAIR ? 256 : 128);
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_ptr, 2 * BN);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc2(tmem_ptr, 2 * BN);
+            tmem_relinquish2();
+        } else {
+            tmem_alloc(tmem_ptr, 2 * BN);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();   // both CTAs' barriers exist before either signals the other
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_ptr;
-    __shared__ int s_abort_store;
-    volatile int* s_abort = &s_abort_store;
-    if (threadIdx.x == 0) *s_abort = 0;
-    __syncthreads();
 
     if (warp == 0) {
-        // ---------------- TMA producer
+        // ---------------- TMA producer (in both CTAs of a pair)
         if (lane == 0) {
             int it = 0;
             for (int ct = 0; ct < ntiles && !*s_abort; ++ct) {
@@ -473,21 +553,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                     const uint32_t ph = (it / STAGES) & 1;
                     if (!mbar_wait_sleep(&empty[st], ph ^ 1)) { *s_abort = 1; break; }
                     char* base = sm + st * Ly::STAGE;
-                    mbar_expect_tx(&full[st], Ly::STAGE);
                     const int k0 = ks * KELEM;
-                    tma_load_2d(base, &tmA, k0, (int)rb0, &full[st]);
-                    tma_load_2d(base + Ly::A_BYTES, &tmB, k0, ct * BN, &full[st]);
-                    if constexpr (MODE == MODE_TF32X3) {
-                        tma_load_2d(base + Ly::A_BYTES + Ly::B_BYTES, &tmA2, k0, (int)rb0, &full[st]);
-                        tma_load_2d(base + 2 * Ly::A_BYTES + Ly::B_BYTES, &tmB2, k0, ct * BN, &full[st]);
+                    if constexpr (PAIR) {
+                        // the leader's barrier counts both CTAs' bytes
+                        if (leader) mbar_expect_tx(&full[st], 2 * Ly::STAGE);
+                        const uint32_t fb = cluster_addr(&full[st], 0);
+                        const int bcol = ct * BN + (int)rank * Ly::B_ROWS;
+                        tma_load_2d_pair(base, &tmA, k0, (int)rb0, fb);
+                        tma_load_2d_pair(base + Ly::A_BYTES, &tmB, k0, bcol, fb);
+                        if constexpr (MODE == MODE_TF32X3) {
+                            tma_load_2d_pair(base + Ly::A_BYTES + Ly::B_BYTES, &tmA2, k0, (int)rb0, fb);
+                            tma_load_2d_pair(base + 2 * Ly::A_BYTES + Ly::B_BYTES, &tmB2, k0, bcol, fb);
+                        }
+                    } else {
+                        mbar_expect_tx(&full[st], Ly::STAGE);
+                        tma_load_2d(base, &tmA, k0, (int)rb0, &full[st]);
+                        tma_load_2d(base + Ly::A_BYTES, &tmB, k0, ct * BN, &full[st]);
+                        if constexpr (MODE == MODE_TF32X3) {
+                            tma_load_2d(base + Ly::A_BYTES + Ly::B_BYTES, &tmA2, k0, (int)rb0, &full[st]);
+                            tma_load_2d(base + 2 * Ly::A_BYTES + Ly::B_BYTES, &tmB2, k0, ct * BN, &full[st]);
+                        }
                     }
                 }
             }
         }
         __syncwarp();   // reconverge before the block-wide barrier below
     } else if (warp == 1) {
-        // ---------------- MMA issuer
-        if (lane == 0) {
+        // ---------------- MMA issuer (the leader of a pair only)
+        if (lane == 0 && leader) {
             int it = 0;
             for (int ct = 0; ct < ntiles && !*s_abort; ++ct) {
                 const int acc = ct & 1;
@@ -504,17 +597,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
 #pragma unroll
                     for (int k = 0; k < KSUB; ++k) {
                         const uint32_t first = (ks == 0 && k == 0) ? 0u : 1u;
-                        umma<MODE>(dtm, smem_desc(a_hi + 32 * k), smem_desc(b_hi + 32 * k), IDESC, first);
+                        const uint64_t ah = smem_desc(a_hi + 32 * k), bh = smem_desc(b_hi + 32 * k);
+                        if constexpr (PAIR) umma_pair<MODE>(dtm, ah, bh, IDESC, first);
+                        else umma<MODE>(dtm, ah, bh, IDESC, first);
                         if constexpr (MODE == MODE_TF32X3) {
                             const char* a_lo = base + Ly::A_BYTES + Ly::B_BYTES;
                             const char* b_lo = base + 2 * Ly::A_BYTES + Ly::B_BYTES;
-                            umma<MODE>(dtm, smem_desc(a_hi + 32 * k), smem_desc(b_lo + 32 * k), IDESC, 1u);
-                            umma<MODE>(dtm, smem_desc(a_lo + 32 * k), smem_desc(b_hi + 32 * k), IDESC, 1u);
+                            const uint64_t al = smem_desc(a_lo + 32 * k), bl = smem_desc(b_lo + 32 * k);
+                            if constexpr (PAIR) {
+                                umma_pair<MODE>(dtm, ah, bl, IDESC, 1u);
+                                umma_pair<MODE>(dtm, al, bh, IDESC, 1u);
+                            } else {
+                                umma<MODE>(dtm, ah, bl, IDESC, 1u);
+                                umma<MODE>(dtm, al, bh, IDESC, 1u);
+                            }
                         }
                     }
-                    umma_commit(&empty[st]);
+                    if constexpr (PAIR) umma_commit_pair(&empty[st]);
+                    else umma_commit(&empty[st]);
                 }
-                umma_commit(&accf[acc]);
+                if constexpr (PAIR) umma_commit_pair(&accf[acc]);
+                else umma_commit(&accf[acc]);
             }
         }
         __syncwarp();
@@ -538,7 +641,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                     norms_s[acc * BN + c] = (j < P.n) ? __ldg(&P.norms[j]) : 0.f;
                 }
             }
-            const bool ok = mbar_wait_sleep(&accf[acc], (ct >> 1) & 1);
+            const bool ok = !*s_abort && mbar_wait_sleep(&accf[acc], (ct >> 1) & 1);
             if (!epi_all(ok && !*s_abort)) {   // also publishes the norms written above
                 *s_abort = 1;
                 break;
@@ -553,7 +656,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 32, v);
                 if (ch == BN / 32 - 1) {
                     tc_fence_before();
-                    mbar_arrive(&acce[acc]);
+                    if constexpr (PAIR) mbar_arrive_cluster(cluster_addr(&acce[acc], 0));
+                    else mbar_arrive(&acce[acc]);
                 }
 #pragma unroll
                 for (int g = 0; g < 32 / GROUP; ++g) {
@@ -596,11 +700,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) sweep_kernel(const __grid_constan
         }
     }
     tc_fence_before();
-    __syncthreads();
-    if (*s_abort && threadIdx.x == 0 && P.status) atomicExch(P.status, ERR_TIMEOUT);
+    if constexpr (PAIR) cluster_sync();   // nothing of the pair is still in flight to either CTA
+    else __syncthreads();
+    if (*s_abort && threadIdx.x == 0 && P.status) atomicExch(P.status, *s_abort == 2 ? SWB_ERR_SMEM : ERR_TIMEOUT);
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * BN);
+        if constexpr (PAIR) tmem_dealloc2(tmem, 2 * BN);
+        else tmem_dealloc(tmem, 2 * BN);
     }
 }
 
@@ -658,17 +764,20 @@ int make_map(CUtensorMap* m, const void* base, int64_t n, int dim, int esize, in
     return SWB_OK;
 }
 
-template <int MODE>
+// rows of the workspace's per-row lists: a whole number of CTA pairs
+int64_t padded_rows(int64_t rows) { return (rows + 2 * BM - 1) / (2 * BM) * (2 * BM); }
+
+template <int MODE, bool PAIR>
 int launch_sweep(const void* a_hi, const void* a_lo, int64_t n, int dim, const float* norms, int64_t row0,
                  int64_t rows, int C, int metric, int32_t* idx, float* dst, void* ws, int32_t* status,
                  cudaStream_t st) {
-    using Ly = Layout<MODE>;
+    using Ly = Layout<MODE, PAIR>;
     const int esize = (MODE == MODE_F16) ? 2 : 4;
     CUtensorMap mA, mA2, mB, mB2;
     int rc = make_map(&mA, a_hi, n, dim, esize, BM);
-    if (!rc) rc = make_map(&mB, a_hi, n, dim, esize, Cfg<MODE>::BN);
+    if (!rc) rc = make_map(&mB, a_hi, n, dim, esize, Ly::B_ROWS);
     if (!rc) rc = make_map(&mA2, a_lo ? a_lo : a_hi, n, dim, esize, BM);
-    if (!rc) rc = make_map(&mB2, a_lo ? a_lo : a_hi, n, dim, esize, Cfg<MODE>::BN);
+    if (!rc) rc = make_map(&mB2, a_lo ? a_lo : a_hi, n, dim, esize, Ly::B_ROWS);
     if (rc) return rc;
     Params P;
     P.n = n;
@@ -679,23 +788,40 @@ int launch_sweep(const void* a_hi, const void* a_lo, int64_t n, int dim, const f
     P.metric = metric;
     P.norms = norms;
     P.best_d = reinterpret_cast<float*>(ws);
-    P.best_i = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) + (size_t)((rows + BM - 1) / BM) * BM * 2 * C * 4);
+    P.best_i = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) + (size_t)padded_rows(rows) * 2 * C * 4);
     P.idx = idx;
     P.dst = dst;
     P.status = status;
     const int smem = Ly::ALLOC;
-    cudaError_t e = cudaFuncSetAttribute(sweep_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(sweep_kernel<MODE, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute(sweep)");
-    const unsigned blocks = (unsigned)((rows + BM - 1) / BM);
-    sweep_kernel<MODE><<<blocks, NTHREADS, smem, st>>>(mA, mA2, mB, mB2, P);
+    unsigned blocks = (unsigned)((rows + BM - 1) / BM);
+    if (!PAIR) {
+        sweep_kernel<MODE, false><<<blocks, NTHREADS, smem, st>>>(mA, mA2, mB, mB2, P);
+        return abi::cuda_check("sweep launch");
+    }
+    blocks += blocks & 1u;   // whole pairs; a spare CTA has no live rows
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, sweep_kernel<MODE, true>, mA, mA2, mB, mB2, P);
+    if (e != cudaSuccess) return abi::cuda_fail(e, "sweep launch (CTA pairs)");
     return abi::cuda_check("sweep launch");
 }
 
 }  // namespace
 
 extern "C" uint64_t swb_sweep_workspace(int64_t n, int64_t rows, int C, int x_dtype) {
-    const int64_t padded = (rows + BM - 1) / BM * BM;
-    uint64_t b = (uint64_t)padded * 2 * C * 8;                 // ping-pong best lists
+    uint64_t b = (uint64_t)padded_rows(rows) * 2 * C * 8;      // ping-pong best lists
     if (x_dtype == SWB_F32) b += 2 * (uint64_t)n * 0;          // hi / lo planes are caller-provided
     (void)n;
     return b;
@@ -721,13 +847,19 @@ extern "C" int swb_sweep_topc(const void* X, const void* X_lo, int x_dtype, int6
     if (reinterpret_cast<uintptr_t>(X) % 16 || (X_lo && reinterpret_cast<uintptr_t>(X_lo) % 16))
         return abi::fail(SWB_ERR_ARG, "rows must be 16-byte aligned");
     cudaStream_t st = (cudaStream_t)stream;
+    // CTA pairs (M = 256 across two SMs) by default; SWB_SWEEP_PAIR=0 runs one CTA per 128 rows
+    const bool pair = abi::env_int("SWB_SWEEP_PAIR", 1) != 0;
     if (x_dtype == SWB_F16) {
         if (dim % 64) return abi::fail(SWB_ERR_ARG, "the tensor-core sweep needs dim %% 64 == 0 for fp16 rows");
-        return launch_sweep<MODE_F16>(X, nullptr, n, dim, norms, row0, rows, C, metric, idx, dst, workspace, status,
-                                      st);
+        return pair ? launch_sweep<MODE_F16, true>(X, nullptr, n, dim, norms, row0, rows, C, metric, idx, dst,
+                                                   workspace, status, st)
+                    : launch_sweep<MODE_F16, false>(X, nullptr, n, dim, norms, row0, rows, C, metric, idx, dst,
+                                                    workspace, status, st);
     }
     if (!X_lo) return abi::fail(SWB_ERR_ARG, "fp32 rows need their tf32 low parts (swb_split_tf32)");
     if (dim % 32) return abi::fail(SWB_ERR_ARG, "the tensor-core sweep needs dim %% 32 == 0 for fp32 rows");
-    return launch_sweep<MODE_TF32X3>(X, X_lo, n, dim, norms, row0, rows, C, metric, idx, dst, workspace, status,
-                                     st);
+    return pair ? launch_sweep<MODE_TF32X3, true>(X, X_lo, n, dim, norms, row0, rows, C, metric, idx, dst, workspace,
+                                                  status, st)
+                : launch_sweep<MODE_TF32X3, false>(X, X_lo, n, dim, norms, row0, rows, C, metric, idx, dst, workspace,
+                                                   status, st);
 }
