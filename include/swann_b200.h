@@ -223,9 +223,14 @@ SWB_API int swb_row_norms(const void* X, int x_dtype, int64_t n, int dim, float*
  * unless an already-kept j has alpha * pair(j, i) <= cdist[u, i]; at most `deg`
  * kept, written in candidate order and padded with -1.
  *   X [n, dim] f32 rows (fp16 corpora are built in fp32, build.py:165-166)
- *   cand/cdist [rows, C] int32 / float32, C <= 128;  out [rows, deg] int32 */
+ *   cand/cdist [rows, C] int32 / float32, C <= 128;  out [rows, deg] int32
+ *   deg_per_node  optional int32 [rows]: node u keeps at most min(deg_per_node[u],
+ *                 deg) (robust_prune's deg_per_node; deg is then the widest)
+ *   protect       optional uint8 [rows, C]: a set entry exempts that candidate
+ *                 from the detour test (robust_prune's protect, mutual pairs) */
 SWB_API int swb_prune(const float* X, int64_t n, int dim, const int32_t* cand, const float* cdist,
-              int64_t rows, int C, int deg, float alpha, int metric, int32_t* out, void* stream);
+              int64_t rows, int C, int deg, float alpha, int metric,
+              const int32_t* deg_per_node, const uint8_t* protect, int32_t* out, void* stream);
 
 /* Replaces add_reverse (swann/build.py:96-150): offers every edge of G back to
  * its target (first `max_in` offers per target in source order), merges with
@@ -233,11 +238,42 @@ SWB_API int swb_prune(const float* X, int64_t n, int dim, const int32_t* cand, c
  * 128 and re-prunes to `deg` -- for rows [row0, row0 + rows) (a rank's row
  * block; the whole graph is row0 = 0, rows = n).
  *   G [n, deg] int32;  out [rows, deg] int32 (must not alias G)
+ *   deg_per_node  optional int32 [n] per-node caps of the re-prune (add_reverse's
+ *                 deg_per_node), indexed by node id
  *   workspace: at least swb_reverse_workspace(n, rows, deg, max_in) bytes */
 SWB_API int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G, int deg, float alpha,
-                int max_in, int metric, int64_t row0, int64_t rows, int32_t* out,
-                void* workspace, uint64_t ws_bytes, void* stream);
+                int max_in, int metric, const int32_t* deg_per_node, int64_t row0, int64_t rows,
+                int32_t* out, void* workspace, uint64_t ws_bytes, void* stream);
 SWB_API uint64_t swb_reverse_workspace(int64_t n, int64_t rows, int deg, int max_in);
+
+/* ------------------------------------------------- offline builder extras -- */
+
+/* Replaces candidates_from_graph (offline/build_graph.py:73-99): node u's
+ * first C entries of an existing graph Gc [n, gc_width], with exact distances
+ * (dimension-ordered fmaf), -1 entries and u itself at 3.4e38, ordered by
+ * (distance, position).  X [n, dim] f32; idx [n, C] int32, dst [n, C] f32. */
+SWB_API int swb_graph_candidates(const float* X, int64_t n, int dim, const int32_t* Gc, int gc_width, int C,
+                         int metric, int32_t* idx, float* dst, void* stream);
+
+/* Replaces mutual_rank (offline/build_graph.py:102-130): out[u, i] = 1 when
+ * i < M, cand[u, i] >= 0 and u is among the first M entries of
+ * cand[cand[u, i]]; cand [n, C] int32, out [n, C] uint8. */
+SWB_API int swb_mutual_rank(const int32_t* cand, int64_t n, int C, int M, uint8_t* out, void* stream);
+
+/* Replaces fill_degree (offline/build_graph.py:133-202), in place on G [n, W]:
+ * rule 0 "near", 1 "far", 2 "bridge"; rows `chunk` at a time, each chunk
+ * seeing the earlier chunks' fills; tmp [chunk, W] int32 scratch. */
+SWB_API int swb_fill_degree(int32_t* G, int64_t n, int W, const int32_t* cand, int C, int rule, int chunk,
+                    int32_t* tmp, void* stream);
+
+/* Replaces enforce_min_in (offline/build_graph.py:309-386), in place on G
+ * [n, W]: up to `rounds` rounds of offering nodes below `min_in` in-edges to
+ * their candidates (cand [n, C]).  Synchronous (it stops when the floor is
+ * met).  stats: optional host int32 [rounds][4] (nodes below, edges to place,
+ * placed, already linked); rounds_run: optional host int. */
+SWB_API uint64_t swb_min_in_workspace(int64_t n);
+SWB_API int swb_enforce_min_in(int32_t* G, int64_t n, int W, const int32_t* cand, int C, int min_in, int rounds,
+                       void* workspace, uint64_t ws_bytes, int32_t* stats, int* rounds_run, void* stream);
 
 /* --------------------------------------------------------------- utility -- */
 

@@ -66,11 +66,11 @@ def _declare(L):
     L.or_knn_candidates.restype = i32
     L.or_knn_candidates.argtypes = [vp, i64, i32, i32, i32, i64, i64, i32, vp, vp, vp]
     L.or_robust_prune.restype = i32
-    L.or_robust_prune.argtypes = [vp, i64, i32, vp, vp, i32, i32, f32, i32, i32, vp]
+    L.or_robust_prune.argtypes = [vp, i64, i32, vp, vp, i32, i32, f32, i32, vp, vp, i32, vp]
     L.or_set_square_mode.restype = None
     L.or_set_square_mode.argtypes = [i32]
     L.or_add_reverse.restype = i32
-    L.or_add_reverse.argtypes = [vp, i64, i32, vp, i32, f32, i32, i32, i32, vp]
+    L.or_add_reverse.argtypes = [vp, i64, i32, vp, i32, f32, i32, i32, vp, i32, vp]
 
 
 def _f32(a):
@@ -163,19 +163,27 @@ def knn_candidates(X, C, metric=METRIC_IP, rows=None, threads=0, exact64=False):
     return (idx, dst, d64) if exact64 else (idx, dst)
 
 
-def robust_prune(X, cand, cdist, deg, alpha=1.2, metric=METRIC_IP, threads=0):
+def robust_prune(X, cand, cdist, deg, alpha=1.2, metric=METRIC_IP, threads=0, deg_per_node=None, protect=None):
+    """deg_per_node: per-node caps (the width is then their largest);
+    protect: bool [n, C] candidates exempt from the detour test."""
     X, cand, cdist = _f32(X), _i32(cand), _f32(cdist)
-    out = np.empty((cand.shape[0], deg), np.int32)
+    dpn = None if deg_per_node is None else _i32(deg_per_node)
+    width = int(deg) if dpn is None else int(dpn.max())
+    prot = None if protect is None else np.ascontiguousarray(protect, dtype=np.uint8)
+    out = np.empty((cand.shape[0], width), np.int32)
     lib().or_robust_prune(_p(X), cand.shape[0], X.shape[1], _p(cand), _p(cdist), cand.shape[1],
-                          deg, float(alpha), metric, threads, _p(out))
+                          width, float(alpha), metric, _p(dpn) if dpn is not None else None,
+                          _p(prot) if prot is not None else None, threads, _p(out))
     return out
 
 
-def add_reverse(X, G, deg, alpha=1.2, max_in=64, metric=METRIC_IP, threads=0):
+def add_reverse(X, G, deg, alpha=1.2, max_in=64, metric=METRIC_IP, threads=0, deg_per_node=None):
+    """deg_per_node: per-node caps of the re-prune; G's width is their largest."""
     X, G = _f32(X), _i32(G)
-    out = np.empty((G.shape[0], deg), np.int32)
+    dpn = None if deg_per_node is None else _i32(deg_per_node)
+    out = np.empty((G.shape[0], G.shape[1]), np.int32)
     lib().or_add_reverse(_p(X), X.shape[0], X.shape[1], _p(G), G.shape[1], float(alpha), max_in,
-                         metric, threads, _p(out))
+                         metric, _p(dpn) if dpn is not None else None, threads, _p(out))
     return out
 
 

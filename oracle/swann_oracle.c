@@ -582,8 +582,11 @@ static float l2_seq(const float* a, const float* b, int d) {
  * pair(j,i) = 1 - <v_j,v_i> (ip) or ((|v_i|^2 - 2<v_j,v_i>) + |v_j|^2) clamped
  * at 0 (l2) -- the reference's expression, element [j][i] of its bmm form.
  * alpha is applied in fp32, as torch does for a python scalar. */
+/* deg: this node's cap; width: the output row's width; prot (optional): a set
+ * entry exempts that candidate from the detour test (robust_prune's protect,
+ * offline/build_graph.py:230-232) */
 static void prune_one(const float* X, int d, const int* cand, const float* du, int C,
-                      int deg, int width, float alpha, int metric, int* out,
+                      int deg, int width, float alpha, int metric, const uint8_t* prot, int* out,
                       float* vn, uint8_t* kept) {
     for (int i = 0; i < C; ++i) {
         vn[i] = 0.0f;
@@ -609,6 +612,7 @@ static void prune_one(const float* X, int d, const int* cand, const float* du, i
             }
             if (alpha * pr <= du[i]) viol = 1;
         }
+        if (prot && prot[i]) viol = 0;
         if (!viol) { kept[i] = 1; ++nk; }
     }
     int w = 0;
@@ -617,8 +621,10 @@ static void prune_one(const float* X, int d, const int* cand, const float* du, i
     for (; w < width; ++w) out[w] = -1;
 }
 
+/* deg is the output width; dpn (optional) caps node u at min(dpn[u], deg) */
 int or_robust_prune(const float* X, int64_t n, int d, const int* cand, const float* cdist, int C,
-                    int deg, float alpha, int metric, int nthreads, int* out) {
+                    int deg, float alpha, int metric, const int* dpn, const uint8_t* prot, int nthreads,
+                    int* out) {
 #ifdef _OPENMP
     if (nthreads > 0) omp_set_num_threads(nthreads);
 #pragma omp parallel
@@ -630,8 +636,9 @@ int or_robust_prune(const float* X, int64_t n, int d, const int* cand, const flo
 #pragma omp for schedule(dynamic, 16)
 #endif
         for (int64_t u = 0; u < n; ++u)
-            prune_one(X, d, cand + (size_t)u * C, cdist + (size_t)u * C, C, deg, deg, alpha, metric,
-                      out + (size_t)u * deg, vn, kept);
+            prune_one(X, d, cand + (size_t)u * C, cdist + (size_t)u * C, C,
+                      dpn ? (dpn[u] < deg ? dpn[u] : deg) : deg, deg, alpha, metric,
+                      prot ? prot + (size_t)u * C : NULL, out + (size_t)u * deg, vn, kept);
         free(vn);
         free(kept);
     }
@@ -658,7 +665,7 @@ static int fpair_cmp(const void* a, const void* b) {
  * by id first and the order is stable), cut to 128 and re-pruned.  Slots with
  * no entry carry id 0 and distance +inf into the prune, as in the reference. */
 int or_add_reverse(const float* X, int64_t n, int d, const int* G, int deg, float alpha,
-                   int max_in, int metric, int nthreads, int* out) {
+                   int max_in, int metric, const int* dpn, int nthreads, int* out) {
     /* reverse lists in (source, slot) order */
     int* cnt = (int*)calloc((size_t)n, sizeof(int));
     for (int64_t u = 0; u < n; ++u)
@@ -716,7 +723,8 @@ int or_add_reverse(const float* X, int64_t n, int d, const int* G, int deg, floa
             }
             qsort(fp, (size_t)width, sizeof(fpair_t), fpair_cmp);
             for (int i = 0; i < keepn; ++i) { cand[i] = fp[i].id; cd[i] = fp[i].d; }
-            prune_one(X, d, cand, cd, keepn, deg, deg, alpha, metric, out + (size_t)t * deg, vn, kept);
+            prune_one(X, d, cand, cd, keepn, dpn ? (dpn[t] < deg ? dpn[t] : deg) : deg, deg, alpha, metric,
+                      NULL, out + (size_t)t * deg, vn, kept);
         }
         free(row); free(fp); free(cand); free(cd); free(vn); free(kept);
     }

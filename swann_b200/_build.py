@@ -16,7 +16,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libswann_b200.so"
-SOURCES = ["search.cu", "build.cu", "sweep_mma.cu", "select.cu"]
+SOURCES = ["search.cu", "build.cu", "sweep_mma.cu", "select.cu", "offline.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -32,6 +32,11 @@ SIGNATURES = {
                                   _i32, _f32, _vp, _i32, _vp, _vp, _vp, _f32, _i32, _vp, _vp]),
     "swb_merge_branches": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     "swb_search_prepare": (_i32, [_i32, _vp, _i32, _vp, _vp, _vp]),
+    "swb_graph_candidates": (_i32, [_vp, _i64, _i32, _vp, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "swb_mutual_rank": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp]),
+    "swb_fill_degree": (_i32, [_vp, _i64, _i32, _vp, _i32, _i32, _i32, _vp, _vp]),
+    "swb_min_in_workspace": (_u64, [_i64]),
+    "swb_enforce_min_in": (_i32, [_vp, _i64, _i32, _vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp, _vp]),
     "swb_select_topk": (_i32, [_vp, _i64, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _vp]),
     "swb_search_fused": (_i32, [_vp, _i32, _i64, _i32, _vp, _i32, _vp, _vp,
                                 _i32, _i32, _i32, _i32, _i32, _i32,
@@ -47,8 +52,8 @@ SIGNATURES = {
                               _vp, _vp]),
     "swb_sweep_workspace": (_u64, [_i64, _i64, _i32, _i32]),
     "swb_split_tf32": (_i32, [_vp, _i64, _vp, _vp, _vp]),
-    "swb_prune": (_i32, [_vp, _i64, _i32, _vp, _vp, _i64, _i32, _i32, _f32, _i32, _vp, _vp]),
-    "swb_reverse": (_i32, [_vp, _i64, _i32, _vp, _i32, _f32, _i32, _i32, _i64, _i64, _vp, _vp, _u64, _vp]),
+    "swb_prune": (_i32, [_vp, _i64, _i32, _vp, _vp, _i64, _i32, _i32, _f32, _i32, _vp, _vp, _vp, _vp]),
+    "swb_reverse": (_i32, [_vp, _i64, _i32, _vp, _i32, _f32, _i32, _i32, _vp, _i64, _i64, _vp, _vp, _u64, _vp]),
     "swb_reverse_workspace": (_u64, [_i64, _i64, _i32, _i32]),
     "swb_last_error": (C.c_char_p, []),
     "swb_version": (_i32, []),

@@ -169,17 +169,30 @@ def _knn_mma(Xg, C, metric, half_exact, rows, row_block):
 @torch.no_grad()
 def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None, metric="ip", protect=None):
     """Keep a candidate only when no nearer kept neighbour detours to it
-    (swann/build.py:48-91).  Returns int32 [n, deg], -1 padded."""
-    if deg_per_node is not None or protect is not None:
-        raise NotImplementedError("per-node degrees and protected pairs are not part of this build")
+    (swann/build.py:48-91).  Returns int32 [n, width], -1 padded: width = deg,
+    or the largest of `deg_per_node` (per-node caps, int [n]) when given.
+    `protect` (bool [n, C], e.g. mutual_rank's) exempts a candidate from the
+    detour test."""
     Xf = Xg.float().contiguous()
     cand = cand.to(torch.int32).contiguous()
     cdist = cdist.float().contiguous()
     n, C = cand.shape
-    out = torch.empty((n, deg), dtype=torch.int32, device=Xg.device)
+    width = int(deg)
+    dpn = None
+    if deg_per_node is not None:
+        dpn = deg_per_node.to(device=Xg.device, dtype=torch.int32).contiguous()
+        if dpn.shape != (n,):
+            raise ValueError("deg_per_node must have one entry per node")
+        width = int(dpn.max())
+    prot = None
+    if protect is not None:
+        prot = protect.to(device=Xg.device, dtype=torch.uint8).contiguous()
+        if prot.shape != (n, C):
+            raise ValueError("protect must have the candidate matrix's shape")
+    out = torch.empty((n, width), dtype=torch.int32, device=Xg.device)
     with torch.cuda.device(Xg.device):
-        rc = N.lib().swb_prune(N.ptr(Xf), Xf.shape[0], Xf.shape[1], N.ptr(cand), N.ptr(cdist), n, C, int(deg),
-                               float(alpha), _m(metric), N.ptr(out), N.stream_of(Xg))
+        rc = N.lib().swb_prune(N.ptr(Xf), Xf.shape[0], Xf.shape[1], N.ptr(cand), N.ptr(cdist), n, C, width,
+                               float(alpha), _m(metric), N.ptr(dpn), N.ptr(prot), N.ptr(out), N.stream_of(Xg))
     N.check(rc, "robust_prune")
     return out
 
@@ -188,22 +201,28 @@ def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None,
 def add_reverse(Xg, G, deg, chunk=2048, alpha=1.2, max_in=64, deg_per_node=None, metric="ip", rows=None):
     """Offer every edge back to its target, then re-prune the union per node
     (swann/build.py:96-150).  rows=(r0, r1) re-prunes only those rows (a
-    rank's block of a sharded build); G is always the whole graph."""
-    if deg_per_node is not None:
-        raise NotImplementedError("per-node degrees are not part of this build")
+    rank's block of a sharded build); G is always the whole graph.  With
+    `deg_per_node` (int [n]) the caps are per node and the width is their
+    largest, as robust_prune writes it."""
     Xf = Xg.float().contiguous()
     G = G.to(torch.int32).contiguous()
     n = G.shape[0]
     r0, r1 = (0, n) if rows is None else rows
-    if G.shape[1] != deg:
-        raise ValueError("add_reverse: the graph's width must equal deg")
+    dpn = None
+    width = int(deg)
+    if deg_per_node is not None:
+        dpn = deg_per_node.to(device=Xg.device, dtype=torch.int32).contiguous()
+        width = int(dpn.max())
+    if G.shape[1] != width:
+        raise ValueError("add_reverse: the graph's width must equal deg (the largest per-node degree)")
+    deg = width
     out = torch.empty((r1 - r0, deg), dtype=torch.int32, device=Xg.device)
     lib = N.lib()
     ws_bytes = int(lib.swb_reverse_workspace(n, r1 - r0, G.shape[1], max_in))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=Xg.device)
     with torch.cuda.device(Xg.device):
         rc = lib.swb_reverse(N.ptr(Xf), n, Xf.shape[1], N.ptr(G), int(deg), float(alpha), int(max_in), _m(metric),
-                             r0, r1 - r0, N.ptr(out), N.ptr(ws), ws_bytes, N.stream_of(Xg))
+                             N.ptr(dpn), r0, r1 - r0, N.ptr(out), N.ptr(ws), ws_bytes, N.stream_of(Xg))
     N.check(rc, "add_reverse")
     return out
 

@@ -261,7 +261,10 @@ template <bool VEC>
 __global__ void __launch_bounds__(PR_THREADS, 2) prune_kernel(const float* __restrict__ X, int64_t n, int dim,
                                                              const int32_t* __restrict__ cand,
                                                              const float* __restrict__ cdist, int C, int deg,
-                                                             float alpha, int metric, int32_t* __restrict__ out) {
+                                                             float alpha, int metric,
+                                                             const int32_t* __restrict__ dpn,
+                                                             const uint8_t* __restrict__ protect,
+                                                             int32_t* __restrict__ out) {
     extern __shared__ __align__(128) char smem[];
     float* gram = reinterpret_cast<float*>(smem);                  // [128][128]
     float* stage = gram;                                           // [2][PR_KC][128], during the products
@@ -325,9 +328,13 @@ __global__ void __launch_bounds__(PR_THREADS, 2) prune_kernel(const float* __res
     }
     __syncthreads();
     if (tid < 32) {
+        // deg is the output width; a node's own cap is dpn[u] when per-node
+        // degrees are given (robust_prune's deg_per_node, swann/build.py:48-91)
         const int lane = tid;
+        const int cap = dpn ? min(dpn[u], deg) : deg;
+        const uint8_t* prot = protect ? protect + u * C : nullptr;
         int nk = 0;
-        for (int i = 0; i < C && nk < deg; ++i) {
+        for (int i = 0; i < C && nk < cap; ++i) {
             if (cid[i] < 0) continue;
             bool viol = false;
             const float gii = gram[i * PR_CP + i];
@@ -344,6 +351,7 @@ __global__ void __launch_bounds__(PR_THREADS, 2) prune_kernel(const float* __res
                 if (__fmul_rn(alpha, pr) <= du[i]) viol = true;
             }
             viol = __any_sync(FULL, viol);
+            if (prot && prot[i]) viol = false;   // a protected pair survives the detour test
             if (!viol) {
                 if (lane == 0) kept[i] = 1;
                 ++nk;
@@ -519,20 +527,23 @@ size_t radix_temp_bytes(int64_t total) {
 // n rows of candidates over a corpus of nx rows
 template <bool VEC>
 int launch_prune_t(const float* X, int64_t nx, int64_t n, int dim, const int32_t* cand, const float* cdist, int C,
-                   int deg, float alpha, int metric, int32_t* out, cudaStream_t st) {
+                   int deg, float alpha, int metric, const int32_t* dpn, const uint8_t* protect, int32_t* out,
+                   cudaStream_t st) {
     if (PR_SMEM > abi::max_smem_optin()) return abi::fail(SWB_ERR_SMEM, "prune needs %d B of shared memory", PR_SMEM);
     cudaError_t e = cudaFuncSetAttribute(prune_kernel<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM);
     if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute(prune)");
-    prune_kernel<VEC><<<(unsigned)n, PR_THREADS, PR_SMEM, st>>>(X, nx, dim, cand, cdist, C, deg, alpha, metric, out);
+    prune_kernel<VEC><<<(unsigned)n, PR_THREADS, PR_SMEM, st>>>(X, nx, dim, cand, cdist, C, deg, alpha, metric, dpn,
+                                                               protect, out);
     return abi::cuda_check("prune launch");
 }
 
 int launch_prune(const float* X, int64_t nx, int64_t n, int dim, const int32_t* cand, const float* cdist, int C,
-                 int deg, float alpha, int metric, int32_t* out, cudaStream_t st) {
+                 int deg, float alpha, int metric, const int32_t* dpn, const uint8_t* protect, int32_t* out,
+                 cudaStream_t st) {
     if (C > PR_CP) return abi::fail(SWB_ERR_ARG, "candidates per node must be at most %d", PR_CP);
     const bool vec = (dim % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0);
-    return vec ? launch_prune_t<true>(X, nx, n, dim, cand, cdist, C, deg, alpha, metric, out, st)
-               : launch_prune_t<false>(X, nx, n, dim, cand, cdist, C, deg, alpha, metric, out, st);
+    return vec ? launch_prune_t<true>(X, nx, n, dim, cand, cdist, C, deg, alpha, metric, dpn, protect, out, st)
+               : launch_prune_t<false>(X, nx, n, dim, cand, cdist, C, deg, alpha, metric, dpn, protect, out, st);
 }
 
 }  // namespace
@@ -570,12 +581,14 @@ extern "C" int swb_topc_block(const float* dots, int64_t rows, int64_t ld, int64
 }
 
 extern "C" int swb_prune(const float* X, int64_t n, int dim, const int32_t* cand, const float* cdist, int64_t rows,
-                         int C, int deg, float alpha, int metric, int32_t* out, void* stream) {
+                         int C, int deg, float alpha, int metric, const int32_t* deg_per_node,
+                         const uint8_t* protect, int32_t* out, void* stream) {
     if (!X || !cand || !cdist || !out) return abi::fail(SWB_ERR_ARG, "null buffer");
     if (C < 1 || C > 128) return abi::fail(SWB_ERR_ARG, "candidates per node must be 1..128");
     if (deg < 1) return abi::fail(SWB_ERR_ARG, "degree must be positive");
     if (rows <= 0) return SWB_OK;
-    return launch_prune(X, n, rows, dim, cand, cdist, C, deg, alpha, metric, out, (cudaStream_t)stream);
+    return launch_prune(X, n, rows, dim, cand, cdist, C, deg, alpha, metric, deg_per_node, protect, out,
+                        (cudaStream_t)stream);
 }
 
 extern "C" uint64_t swb_reverse_workspace(int64_t n, int64_t rows, int deg, int max_in) {
@@ -590,8 +603,8 @@ extern "C" uint64_t swb_reverse_workspace(int64_t n, int64_t rows, int deg, int 
 }
 
 extern "C" int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G, int deg, float alpha, int max_in,
-                           int metric, int64_t row0, int64_t rows, int32_t* out, void* workspace, uint64_t ws_bytes,
-                           void* stream) {
+                           int metric, const int32_t* deg_per_node, int64_t row0, int64_t rows, int32_t* out,
+                           void* workspace, uint64_t ws_bytes, void* stream) {
     if (!X || !G || !out || !workspace) return abi::fail(SWB_ERR_ARG, "null buffer");
     if (n <= 0 || rows <= 0) return SWB_OK;
     if (row0 < 0 || row0 + rows > n) return abi::fail(SWB_ERR_ARG, "row range outside the graph");
@@ -632,7 +645,8 @@ extern "C" int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G,
                                                                n, row0, cand, cdist);
     rc = abi::cuda_check("reverse merge launch");
     if (rc) return rc;
-    return launch_prune(X, n, rows, dim, cand, cdist, keepn, deg, alpha, metric, out, st);
+    return launch_prune(X, n, rows, dim, cand, cdist, keepn, deg, alpha, metric,
+                        deg_per_node ? deg_per_node + row0 : nullptr, nullptr, out, st);
 }
 
 extern "C" const char* swb_last_error(void) { return abi::last_error().c_str(); }
