@@ -28,7 +28,7 @@
  *     separately rounded products, then the halving tree;
  *   - build dot products are sequential fmaf over the dimension (the reference
  *     leaves this order to BLAS, which specifies none); the exact candidate
- *     sweep uses double precision so that it is the "truth" ties are judged by.
+ *     sweep uses double precision so that it is the "truth" ties are measured against.
  *
  * Build: gcc -O2 -fPIC -shared -ffp-contract=off -fno-builtin-powf -fopenmp
  * (oracle/build_oracle.py).
@@ -511,8 +511,8 @@ int or_search(const float* X, int64_t n, int d, const int* G, int D,
  * (distance, id).  swann/build.py:14-43.  The reference evaluates
  * 1 - <a,b> (ip) or (|b|^2 - 2<a,b>) + |a|^2 clamped at 0 (l2) from an fp32
  * GEMM and marks the diagonal 3.4e38; here the same expressions are evaluated
- * in double, so these lists are the exact answer that fp32 results are judged
- * against.  Rows [r0, r1) only (a row sample of a large sweep). */
+ * in double, so these lists are the exact answer that fp32 results are
+ * compared with.  Rows [r0, r1) only (a row sample of a large sweep). */
 typedef struct { double d; int id; } dpair_t;
 static int dpair_cmp(const void* a, const void* b) {
     const dpair_t* x = (const dpair_t*)a;

@@ -190,34 +190,13 @@ __device__ __forceinline__ int visited_insert(int* tab, int H, int v, int& fail)
 }
 
 // Per-query distance table slot = (id + 1) << 32 | float bits; a claimed but
-// not yet scored slot carries FLT_MAX.  Returns the cached distance (FLT_MAX
-// when none), the slot (-1 after CPROBE probes) and whether this call claimed it.
-__device__ __forceinline__ float cache_probe(uint64_t* tab, int Hc, int v, int& slot, int& claimed) {
-    const uint32_t mask = (uint32_t)(Hc - 1);
-    uint32_t pos = knuth(v, mask);
-    const uint32_t key = (uint32_t)(v + 1);
-    const unsigned long long want = ((unsigned long long)key << 32) | FLT_MAX_BITS;
-    for (int p = 0; p < CPROBE; ++p) {
-        const unsigned long long old = atomicCAS(reinterpret_cast<unsigned long long*>(&tab[pos]), 0ull, want);
-        if (old == 0ull) {
-            slot = (int)pos;
-            claimed = 1;
-            return FLT_MAX;
-        }
-        if ((uint32_t)(old >> 32) == key) {
-            slot = (int)pos;
-            claimed = 0;
-            return __uint_as_float((uint32_t)old);
-        }
-        pos = (pos + 1) & mask;
-    }
-    slot = -1;
-    claimed = 0;
-    return FLT_MAX;
-}
+// not yet scored slot carries FLT_MAX.
 
-// cache_probe given the outcome of its first compare-and-swap (issued by the
-// caller alongside others): resolves it and probes on after a collision
+// One node's probe of the per-query table, given the outcome of its first
+// compare-and-swap (issued by the caller alongside the other neighbours'):
+// resolves it and probes on linearly after a collision (CPROBE probes at
+// most).  Returns the cached distance (FLT_MAX when none), the slot (-1 when
+// the probes ran out) and whether this call claimed it.
 __device__ __forceinline__ float cache_probe_rest(uint64_t* tab, int Hc, int v, uint32_t pos,
                                                   unsigned long long old, int& slot, int& claimed) {
     const uint32_t mask = (uint32_t)(Hc - 1);
