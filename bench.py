@@ -471,6 +471,10 @@ def run(args):
     # -- roofline of the dominant kernel (the fused search) ----------------
     ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
     seeds = index.catalogue[ent].to(torch.int32)
+    from swann_b200 import index as I
+    if index.locality and batch >= I.LOCALITY_MIN:   # the order Index.search runs the batch in
+        order = torch.argsort(ent[:, 0], stable=True)
+        Q, seeds = Q[order].contiguous(), seeds[order].contiguous()
     kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=index._m, team_size=16, stop_eps=op["stop_eps"],
               shared_cache=True, shared_bound=True, exclusive=2, elide_visited=True, table_slots=slots)
     _, _, ctr, _ = E.search_fused_lean(X, G, Q, seeds, **kw)
@@ -542,6 +546,7 @@ def run(args):
                    "recall_sample": gt_n, "graph": "degree 64, candidates 128, alpha 1.2",
                    "catalogue": int(index.catalogue.numel()),
                    "claims": "strict (exclusive=2)", "table": table,
+                   "query_order": "nearest catalogue entry" if index.locality else "input",
                    "l2": "inputs larger than L2 (corpus %.1f GB; rows gathered at random)" % (
                        X.numel() * X.element_size() / 1e9),
                    "parallelism": f"query shards x{world}, replicas"},

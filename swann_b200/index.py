@@ -30,8 +30,10 @@ MAX_BATCH = 65535
 # Bytes of per-query distance tables one launch may use; larger batches are
 # searched in consecutive chunks on the same stream.
 TABLE_BUDGET = 24 << 30
-# host batches larger than this are copied in chunks that overlap the search
+# host batches larger than this are copied in chunks that overlap the seed selection
 COPY_CHUNK = 8192
+# blocks of at least this many queries are searched in locality order (below)
+LOCALITY_MIN = 1024
 
 
 @dataclass
@@ -69,7 +71,7 @@ class Index:
 
     def __init__(self, vectors: torch.Tensor, graph: torch.Tensor, metric: str = "ip",
                  catalogue: torch.Tensor | None = None, catalogue_size: int = 4096, seed: int = 0,
-                 devices=None, table_slots: int | None = None):
+                 devices=None, table_slots: int | None = None, locality: bool = True):
         if vectors.device.type != "cuda":
             raise ValueError("vectors must already be on the GPU")
         if vectors.dtype not in (torch.float32, torch.float16):
@@ -84,6 +86,12 @@ class Index:
         self.G = graph.to(device=self.X.device, dtype=torch.int32).contiguous()
         self.metric = metric
         self._m = METRICS[metric]
+        # Search a large block of queries in the order of their nearest catalogue
+        # entry, so the queries running side by side walk the same part of the
+        # graph and share its rows in L2; the answers go back in input order.
+        # Queries are independent, so this changes when a query runs, not what
+        # it computes.
+        self.locality = bool(locality)
         if catalogue is None:
             n = self.X.shape[0]
             rng = np.random.default_rng(seed)
@@ -139,16 +147,18 @@ class Index:
         host = queries if not isinstance(queries, torch.Tensor) or queries.device.type == "cpu" else None
         if host is not None and isinstance(host, np.ndarray):
             host = torch.from_numpy(np.ascontiguousarray(host))
-        outs = []
+        outs, checks = [], []
         for r, (a, b) in zip(reps, zip(bounds[:-1], bounds[1:])):
             if b <= a:
                 continue
             with torch.cuda.device(r.dev):
                 Hc = self.table_slots or E.cache_size(cfg.branches, cfg.budget, r.G.shape[1])
                 if host is not None and b - a > COPY_CHUNK:
-                    # Host queries: copied chunk by chunk on a side stream, each
-                    # chunk searched while the next one is in flight (the copy
-                    # overlaps the search when the host memory is pinned).
+                    # Host queries: copied chunk by chunk on a side stream; each
+                    # chunk's seeds are selected as it lands (the copies overlap
+                    # the selection when the host memory is pinned), then the
+                    # block is searched as one, so its locality order spans the
+                    # whole block.
                     comp = torch.cuda.current_stream(r.dev)
                     side = self._copy_stream(r.dev)
                     buf = torch.empty((b - a, host.shape[1]), dtype=host.dtype, device=r.dev)
@@ -161,15 +171,21 @@ class Index:
                             ev = torch.cuda.Event()
                             ev.record(side)
                             ready.append((c0, c1, ev))
+                    Qd = buf if buf.dtype == torch.float32 else None
+                    ents = []
                     for c0, c1, ev in ready:
                         comp.wait_event(ev)
-                        self._search_part(r, buf[c0:c1].float().contiguous(), k, cfg, Hc, outs)
+                        ents.append(S.select_nearest(buf[c0:c1].float().contiguous(), r.cat_rows, cfg.branches,
+                                                     metric=self._m))
+                    if Qd is None:
+                        Qd = buf.float().contiguous()
+                    self._search_part(r, Qd, k, cfg, Hc, outs, checks, ent=torch.cat(ents))
                 else:
                     src = host if host is not None else queries
                     Qd = src[a:b].to(r.dev, non_blocking=True).float().contiguous()
-                    self._search_part(r, Qd, k, cfg, Hc, outs)
+                    self._search_part(r, Qd, k, cfg, Hc, outs, checks)
         if E._OVERFLOW_GUARD:
-            for _, _, ctr, status in outs:
+            for ctr, status in checks:
                 if ctr is not None and int(ctr[..., 2].sum()) != 0:
                     raise RuntimeError("visited table overflowed: raise the budget used for sizing")
                 if int(status[0]) != 0:
@@ -179,15 +195,33 @@ class Index:
         dist = torch.cat([o[1].to(dev0) for o in outs]) if outs else torch.empty((0, k))
         return ids, dist
 
-    def _search_part(self, r, Qd, k, cfg, Hc, outs):
+    def _search_part(self, r, Qd, k, cfg, Hc, outs, checks, ent=None):
         """Seed selection and the fused search of one device-resident block of
-        queries, in table-budget sized launches."""
-        ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
+        queries, in table-budget sized launches (and locality order, see
+        `locality`); appends (ids, dist) in input order to `outs` and each
+        launch's (counters, status) to `checks`.  `ent`: the seeds' catalogue
+        indices when already selected."""
+        if ent is None:
+            ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
         seeds = r.catalogue[ent].to(torch.int32)
+        order = None
+        if self.locality and Qd.shape[0] >= LOCALITY_MIN and ent.shape[1] > 0:
+            order = torch.argsort(ent[:, 0], stable=True)
+            Qd, seeds = Qd[order].contiguous(), seeds[order].contiguous()
         step = max(1, min(Qd.shape[0], TABLE_BUDGET // (8 * Hc)))
+        part = []
         for c0 in range(0, Qd.shape[0], step):
             c1 = min(Qd.shape[0], c0 + step)
-            outs.append(_search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc))
+            ids, dist, ctr, status = _search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc)
+            part.append((ids, dist))
+            checks.append((ctr, status))
+        ids = torch.cat([p[0] for p in part]) if len(part) > 1 else part[0][0]
+        dist = torch.cat([p[1] for p in part]) if len(part) > 1 else part[0][1]
+        if order is not None:
+            back = torch.empty_like(order)
+            back[order] = torch.arange(order.numel(), device=order.device)
+            ids, dist = ids[back], dist[back]
+        outs.append((ids, dist))
 
     def _copy_stream(self, dev):
         streams = self.__dict__.setdefault("_copy_streams", {})

@@ -135,3 +135,28 @@ def test_host_batches_larger_than_a_copy_chunk(ip_index):
         dev_ids, _ = idx.search(torch.from_numpy(Q).cuda(), k=10)
         truth = exact(X, Q[sample], 10, "ip")
         assert abs(recall(ids[sample], truth, 10) - recall(dev_ids[sample], truth, 10)) < 0.01
+
+
+def test_locality_order_returns_answers_in_input_order(ip_index):
+    """A block of >= LOCALITY_MIN queries runs grouped by nearest catalogue
+    entry; each answer still comes back at its query's position."""
+    from swann_b200 import index as I
+    X, _, idx = ip_index
+    rng = np.random.default_rng(12)
+    Q = rng.standard_normal((I.LOCALITY_MIN + 500, X.shape[1]), dtype=np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    Qg = torch.from_numpy(Q).cuda()
+    ids_on, dist_on = idx.search(Qg, k=10)
+    idx.locality = False
+    try:
+        ids_off, dist_off = idx.search(Qg, k=10)
+    finally:
+        idx.locality = True
+    sample = np.arange(0, len(Q), 7)
+    for q in sample:
+        exact_d = 1.0 - X[ids_on[q]].astype(np.float64) @ Q[q].astype(np.float64)
+        assert np.allclose(dist_on[q], exact_d, atol=1e-5)
+    truth = exact(X, Q[sample], 10, "ip")
+    assert abs(recall(ids_on[sample], truth, 10) - recall(ids_off[sample], truth, 10)) < 0.01
+    # most queries get the very same answer either way (the branch race aside)
+    assert np.mean((ids_on == ids_off).all(1)) > 0.9
