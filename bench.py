@@ -471,9 +471,8 @@ def run(args):
     # -- roofline of the dominant kernel (the fused search) ----------------
     ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
     seeds = index.catalogue[ent].to(torch.int32)
-    from swann_b200 import index as I
-    if index.locality and batch >= I.LOCALITY_MIN:   # the order Index.search runs the batch in
-        order = torch.argsort(ent[:, 0], stable=True)
+    order = index.locality_order(ent)   # the order Index.search runs the batch in
+    if order is not None:
         Q, seeds = Q[order].contiguous(), seeds[order].contiguous()
     kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=index._m, team_size=16, stop_eps=op["stop_eps"],
               shared_cache=True, shared_bound=True, exclusive=2, elide_visited=True, table_slots=slots)

@@ -104,6 +104,9 @@ class Index:
             devs = [torch.device("cuda", d) if isinstance(d, int) else torch.device(d) for d in devices]
         self._replicas = [_Replica(self.X, self.G, self.catalogue, d) for d in devs]
         self._cat = self._replicas[0].cat_rows
+        self._tour = _catalogue_tour(self._cat, self._m) if self.locality else None
+        for r in self._replicas:
+            r.tour = None if self._tour is None else self._tour.to(r.dev)
         # Slots of each query's distance table.  None: the reference's sizing
         # (swann/_engine.py:186-198).  The table only ever holds the nodes a
         # query's branches score (a few thousand); any power of two that keeps
@@ -204,9 +207,8 @@ class Index:
         if ent is None:
             ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
         seeds = r.catalogue[ent].to(torch.int32)
-        order = None
-        if self.locality and Qd.shape[0] >= LOCALITY_MIN and ent.shape[1] > 0:
-            order = torch.argsort(ent[:, 0], stable=True)
+        order = self.locality_order(ent, r)
+        if order is not None:
             Qd, seeds = Qd[order].contiguous(), seeds[order].contiguous()
         step = max(1, min(Qd.shape[0], TABLE_BUDGET // (8 * Hc)))
         part = []
@@ -222,6 +224,16 @@ class Index:
             back[order] = torch.arange(order.numel(), device=order.device)
             ids, dist = ids[back], dist[back]
         outs.append((ids, dist))
+
+    def locality_order(self, ent, r=None):
+        """The order a block of queries runs in (None: input order), from each
+        query's selected catalogue entries `ent` [nq, E]: by the nearest entry's
+        position on the catalogue's locality tour."""
+        if not self.locality or ent.shape[0] < LOCALITY_MIN or ent.shape[1] == 0:
+            return None
+        tour = (r or self._replicas[0]).tour
+        key = ent[:, 0] if tour is None else tour[ent[:, 0]]
+        return torch.argsort(key, stable=True)
 
     def _copy_stream(self, dev):
         streams = self.__dict__.setdefault("_copy_streams", {})
@@ -254,6 +266,38 @@ class Index:
         n, d = self.X.shape
         return (f"Index(n={n:,}, d={d}, degree={self.G.shape[1]}, metric={self.metric!r}, "
                 f"dtype={self.X.dtype}, devices={len(self._replicas)})")
+
+
+# catalogues up to this size get a locality tour (an O(P^2) pass, once)
+TOUR_MAX = 16384
+
+
+def _catalogue_tour(cat_rows, metric):
+    """Each catalogue entry's position on a greedy nearest-neighbour tour of the
+    catalogue (int64 [P]), or None when the catalogue is too large: sorting
+    queries by their nearest entry's position keeps queries whose entries are
+    close -- not only equal -- side by side."""
+    P = cat_rows.shape[0]
+    if P < 2 or P > TOUR_MAX:
+        return None
+    V = cat_rows.float()
+    with torch.no_grad():
+        if metric == METRICS["ip"]:
+            D = 1.0 - V @ V.T
+        else:
+            vn = (V * V).sum(1)
+            D = vn[:, None] - 2.0 * (V @ V.T) + vn[None, :]
+        D = D.cpu().numpy()
+    pos = np.empty(P, np.int64)
+    seen = np.zeros(P, bool)
+    cur = 0
+    for i in range(P):
+        pos[cur] = i
+        seen[cur] = True
+        if i + 1 < P:
+            row = np.where(seen, np.inf, D[cur])
+            cur = int(np.argmin(row))
+    return torch.from_numpy(pos)
 
 
 def _search_device(r: _Replica, Qd, seeds, k, cfg, metric, table_slots):
