@@ -147,6 +147,30 @@ struct VecN<__half> {
     static constexpr int N = 8;
 };
 
+// Where the query sits in shared memory.  fp32 rows: in order.  fp16 rows (8
+// elements a 16-byte chunk): as two planes, plane h holding elements
+// 8c + 4h .. 8c + 4h + 3 of every chunk c at float offset h * dim / 2 + 4c.
+// The lanes of a team read consecutive chunks, so every 16-byte read of a
+// plane is contiguous across the team; in order, lanes sat 32 bytes apart and
+// each read was a 2-way bank conflict.  part() is the 4 floats for elements
+// c * VecN + 4h ..; pos() the place of element i.
+template <typename XT>
+struct QLay;
+template <>
+struct QLay<float> {
+    static __device__ __forceinline__ const float* part(const float* sq, int, int c, int) { return sq + 4 * c; }
+    static __device__ __forceinline__ int pos(int, int i) { return i; }
+};
+template <>
+struct QLay<__half> {
+    static __device__ __forceinline__ const float* part(const float* sq, int dim, int c, int h) {
+        return sq + h * (dim >> 1) + 4 * c;
+    }
+    static __device__ __forceinline__ int pos(int dim, int i) {
+        return ((i >> 2) & 1) * (dim >> 1) + ((i >> 3) << 2) + (i & 3);
+    }
+};
+
 __device__ __forceinline__ void widen16(const float* p, float* out) {
     const float4 v = *reinterpret_cast<const float4*>(p);
     out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
@@ -193,7 +217,7 @@ __device__ __forceinline__ float team_partial(const float* __restrict__ sq, cons
             float x[V], q[V];
             widen16(row + base, x);
 #pragma unroll
-            for (int i = 0; i < V; i += 4) widen16(sq + base + i, q + i);
+            for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, base / V, i >> 2), q + i);
 #pragma unroll
             for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], x[i]));
         }
@@ -202,7 +226,7 @@ __device__ __forceinline__ float team_partial(const float* __restrict__ sq, cons
             float x[V], q[V];
             widen16(row + base, x);
 #pragma unroll
-            for (int i = 0; i < V; i += 4) widen16(sq + base + i, q + i);
+            for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, base / V, i >> 2), q + i);
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 const float df = __fsub_rn(q[i], x[i]);
@@ -247,7 +271,7 @@ __device__ __forceinline__ float split_partial(const float* __restrict__ sq, con
                     float x[V], q[V];
                     widen16(row + c * V, x);
 #pragma unroll
-                    for (int i = 0; i < V; i += 4) widen16(sq + c * V + i, q + i);
+                    for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, c, i >> 2), q + i);
 #pragma unroll
                     for (int i = 0; i < V; ++i) acc[j] = __fadd_rn(acc[j], __fmul_rn(q[i], x[i]));
                 }
@@ -262,7 +286,7 @@ __device__ __forceinline__ float split_partial(const float* __restrict__ sq, con
                     float x[V], q[V];
                     widen16(row + c * V, x);
 #pragma unroll
-                    for (int i = 0; i < V; i += 4) widen16(sq + c * V + i, q + i);
+                    for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, c, i >> 2), q + i);
 #pragma unroll
                     for (int i = 0; i < V; ++i) {
                         const float df = __fsub_rn(q[i], x[i]);
@@ -319,7 +343,7 @@ __device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, 
                 float x[V], q[V];
                 widen_u4<XT>(raw[u], x);
 #pragma unroll
-                for (int i = 0; i < V; i += 4) widen16(sq + c * V + i, q + i);
+                for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, c, i >> 2), q + i);
                 if (metric == METRIC_IP) {
 #pragma unroll
                     for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], x[i]));

@@ -537,12 +537,14 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
 // x - mu, so <q, b> = 2 * (sum of q over set bits) - sum(q).  The query's two
 // sums are taken once, in a fixed order (the reference adds them with float
 // atomics, whose order varies).
+template <typename XT>
 __device__ __forceinline__ void code_query_sums(const float* sq, const float* cmu, int dim, int lane, float& qmu,
                                                 float& qsum) {
     float a = 0.f, b = 0.f;
     for (int i = lane; i < dim; i += 32) {
-        a = __fadd_rn(a, __fmul_rn(sq[i], cmu[i]));
-        b = __fadd_rn(b, sq[i]);
+        const float qi = sq[QLay<XT>::pos(dim, i)];
+        a = __fadd_rn(a, __fmul_rn(qi, cmu[i]));
+        b = __fadd_rn(b, qi);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -554,7 +556,7 @@ __device__ __forceinline__ void code_query_sums(const float* sq, const float* cm
 }
 
 // The estimated distance 1 - <q, x> of row v, on every lane of its team.
-template <int TEAM>
+template <int TEAM, typename XT>
 __device__ __forceinline__ float code_estimate(const Knobs& K, const float* sq, int v, float qmu, float qsum,
                                                int tl) {
     const uint32_t* code = reinterpret_cast<const uint32_t*>(K.codes) + (size_t)v * K.cwords;
@@ -565,7 +567,7 @@ __device__ __forceinline__ float code_estimate(const Knobs& K, const float* sq, 
 #pragma unroll 8
         for (int b = 0; b < 32; ++b) {
             const int i = base + b;
-            if (i < K.dim && (bits >> b) & 1u) acc = __fadd_rn(acc, sq[i]);
+            if (i < K.dim && (bits >> b) & 1u) acc = __fadd_rn(acc, sq[QLay<XT>::pos(K.dim, i)]);
         }
     }
 #pragma unroll
@@ -578,7 +580,7 @@ __device__ __forceinline__ float code_estimate(const Knobs& K, const float* sq, 
 // beyond `limit` by more than the margin; its vector is never read and its
 // claimed table slot stays unscored.  Returns the rows kept; `skipped` gets
 // the count (on every lane).
-template <int TEAM>
+template <int TEAM, typename XT>
 __device__ int code_filter(const Knobs& K, const WarpMem& w, int m, const float* sq, float limit, float qmu,
                            float qsum, int lane, int& skipped) {
     constexpr int P = 32 / TEAM;
@@ -586,7 +588,7 @@ __device__ int code_filter(const Knobs& K, const WarpMem& w, int m, const float*
     for (int base = 0; base < m; base += P) {
         const int i = base + team;
         const int v = (i < m) ? w.w_v[i] : 0;
-        const float est = code_estimate<TEAM>(K, sq, v, qmu, qsum, tl);
+        const float est = code_estimate<TEAM, XT>(K, sq, v, qmu, qsum, tl);
         if (tl == 0 && i < m) w.w_aux[i] = (est > __fadd_rn(limit, K.cmargin)) ? 1 : 0;
     }
     __syncwarp();
@@ -625,7 +627,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
     int stall = 0, crowd_run = 0;
     if (lane < 8) w.retired[lane] = 0u;
     float qmu = 0.f, qsum = 0.f;
-    if (CODES) code_query_sums(sq, K.cmu, K.dim, lane, qmu, qsum);
+    if (CODES) code_query_sums<XT>(sq, K.cmu, K.dim, lane, qmu, qsum);
     __syncwarp();
 
     for (int step = 0; step < delta; ++step) {
@@ -745,7 +747,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
         __syncwarp();
         if (CODES && limit != FLT_MAX && m > 0) {
             int skipped = 0;
-            m = code_filter<TEAM>(K, w, m, sq, limit, qmu, qsum, lane, skipped);
+            m = code_filter<TEAM, XT>(K, w, m, sq, limit, qmu, qsum, lane, skipped);
             claimed_rows = 0;   // recounted below from the rows actually scored
             for (int b = 0; b < m; b += 32)
                 claimed_rows += __popc(__ballot_sync(FULL, b + lane < m && w.w_slot[b + lane] >= 0));
@@ -842,10 +844,12 @@ __device__ __forceinline__ void ring_setup(const Knobs& K, WarpMem& w, int lane,
     __syncwarp();
 }
 
+// the query into shared memory, in the layout QLay<XT> describes
+template <typename XT>
 __device__ __forceinline__ void load_query(float* sq, const float* src, int dim, int tid, int nthreads) {
     const float4* s4 = reinterpret_cast<const float4*>(src);
     float4* d4 = reinterpret_cast<float4*>(sq);
-    for (int t = tid; t < dim / 4; t += nthreads) d4[t] = __ldg(&s4[t]);
+    for (int t = tid; t < dim / 4; t += nthreads) d4[QLay<XT>::pos(dim, 4 * t) >> 2] = __ldg(&s4[t]);
 }
 
 __device__ void load_state(const Knobs& K, WarpMem& w, size_t bid, int lane, Ctr& ctr) {
@@ -888,7 +892,7 @@ __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs
     WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
     Ring ring;
     ring_setup(K, w, lane, ring);
-    load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
+    load_query<XT>(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
     // the per-query table and bound belong to the query; its J branches clear
     // them between them (local_search.cu:302-313)
     if (K.Hc > 0) {
@@ -922,7 +926,7 @@ __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Kn
     WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
     Ring ring;
     ring_setup(K, w, lane, ring);
-    load_query(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
+    load_query<XT>(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
     Ctr ctr;
     load_state(K, w, (size_t)flat, lane, ctr);
     if (K.codes)
@@ -990,7 +994,7 @@ __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid
     const int j = blockIdx.x * K.W + warp;
     float* sq = reinterpret_cast<float*>(smem);
     const int qbytes = align16(K.dim * 4);
-    load_query(sq, K.Qv + (size_t)q * K.dim, K.dim, threadIdx.x, blockDim.x);
+    load_query<XT>(sq, K.Qv + (size_t)q * K.dim, K.dim, threadIdx.x, blockDim.x);
     __syncthreads();
     if (j >= K.J) return;
     const Layout lay = warp_layout(K.L, K.R, K.rowbytes, 0, K.cmax);
