@@ -18,6 +18,10 @@ CSRC = HERE / "csrc"
 LIB = HERE / "libswann_b200.so"
 SOURCES = ["search.cu", "build.cu", "sweep_mma.cu", "select.cu", "offline.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# The search's distance sums must round every multiply and add on its own (the
+# reference builds with -fmad=false too); ptxas would otherwise fuse the packed
+# f32x2 multiply-adds of the row sums, explicit rounding modifiers or not.
+PER_FILE = {"search.cu": ["-fmad=false"]}
 
 
 def _sources():
@@ -26,7 +30,7 @@ def _sources():
 
 def _deps():
     return _sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + \
-        [HERE.parent / "include" / "swann_b200.h"]
+        [HERE.parent / "include" / "swann_b200.h", Path(__file__).resolve()]
 
 
 def up_to_date() -> bool:
@@ -46,7 +50,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     for src in _sources():
         obj = build_dir / (src.stem + ".o")
         objs.append(obj)
-        cmd = [nvcc] + flags + ["-c", str(src), "-o", str(obj)]
+        cmd = [nvcc] + flags + PER_FILE.get(src.name, []) + ["-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd))
         procs.append(subprocess.Popen(cmd))

@@ -133,8 +133,13 @@ __device__ __forceinline__ unsigned lanemask_lt() {
 // lane l of a TEAM-wide team owns the 16-byte chunks l, l + TEAM, l + 2*TEAM,
 // ... of the row (4 fp32 or 8 fp16 elements each), sums product terms into one
 // fp32 accumulator with the multiply and the add rounded separately, and the
-// team folds its lanes with a shuffle-down tree.  The row arrives here in
-// shared memory instead of straight from HBM; the order is unchanged.
+// team folds its lanes with a shuffle-down tree.  The products of neighbouring
+// elements are formed in pairs (sm_100's mul.rn.f32x2, each half rounded on its
+// own); the sum stays a chain of scalar add.rn, which no compiler pass may fuse
+// with the multiply.  (Chains of packed adds fed by packed multiplies came out
+// of ptxas, in some code shapes, different from separately rounded operations,
+// .rn modifiers and -fmad=false notwithstanding, while each packed operation on
+// its own rounded exactly: measured, so the adds stay scalar.)
 
 template <typename XT>
 struct VecN;
@@ -207,34 +212,19 @@ __device__ __forceinline__ void widen_u4<__half>(const uint4 v, float* out) {
     }
 }
 
-template <int TEAM, typename XT>
-__device__ __forceinline__ float team_partial(const float* __restrict__ sq, const XT* __restrict__ row,
-                                              int dim, int metric, int tl) {
-    constexpr int V = VecN<XT>::N;
-    float acc = 0.f;
-    if (metric == METRIC_IP) {
-        for (int base = tl * V; base < dim; base += TEAM * V) {
-            float x[V], q[V];
-            widen16(row + base, x);
-#pragma unroll
-            for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, base / V, i >> 2), q + i);
-#pragma unroll
-            for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], x[i]));
-        }
-    } else {
-        for (int base = tl * V; base < dim; base += TEAM * V) {
-            float x[V], q[V];
-            widen16(row + base, x);
-#pragma unroll
-            for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, base / V, i >> 2), q + i);
-#pragma unroll
-            for (int i = 0; i < V; ++i) {
-                const float df = __fsub_rn(q[i], x[i]);
-                acc = __fadd_rn(acc, __fmul_rn(df, df));
-            }
-        }
-    }
-    return acc;
+// packed fp32 pairs, each half rounded to nearest on its own
+__device__ __forceinline__ unsigned long long f2_bits(float2 a) {
+    return *reinterpret_cast<const unsigned long long*>(&a);
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    float2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(*reinterpret_cast<unsigned long long*>(&d)) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return d;
+}
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+    float2 d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(*reinterpret_cast<unsigned long long*>(&d)) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return d;
 }
 
 // all 32 lanes call this; each TEAM-wide segment folds independently
@@ -245,67 +235,7 @@ __device__ __forceinline__ float team_reduce(float acc) {
     return acc;
 }
 
-// The same TEAM-lane distance on TP physical lanes (TP divides TEAM).  Physical
-// lane p carries the S = TEAM / TP logical lanes p, p + TP, ..., each with its
-// own accumulator, so one lane runs S independent add chains instead of one.
-// Every logical lane still sums its own chunks in the reference's order, and
-// the tree is unchanged: its levels with offsets >= TP pair logical lanes that
-// share a physical lane (p + j*TP with p + (j + off/TP)*TP) and are done here
-// as local adds of exactly the same operands; split_reduce does the rest with
-// shuffles.  Returns logical lane p's value after the local levels.
-template <int TEAM, int TP, typename XT>
-__device__ __forceinline__ float split_partial(const float* __restrict__ sq, const XT* __restrict__ row, int dim,
-                                               int metric, int p) {
-    constexpr int V = VecN<XT>::N;
-    constexpr int S = TEAM / TP;
-    const int nch = dim / V;
-    float acc[S];
-#pragma unroll
-    for (int j = 0; j < S; ++j) acc[j] = 0.f;
-    if (metric == METRIC_IP) {
-        for (int c0 = 0; c0 < nch; c0 += TEAM) {
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
-                const int c = c0 + p + j * TP;
-                if (c < nch) {
-                    float x[V], q[V];
-                    widen16(row + c * V, x);
-#pragma unroll
-                    for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, c, i >> 2), q + i);
-#pragma unroll
-                    for (int i = 0; i < V; ++i) acc[j] = __fadd_rn(acc[j], __fmul_rn(q[i], x[i]));
-                }
-            }
-        }
-    } else {
-        for (int c0 = 0; c0 < nch; c0 += TEAM) {
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
-                const int c = c0 + p + j * TP;
-                if (c < nch) {
-                    float x[V], q[V];
-                    widen16(row + c * V, x);
-#pragma unroll
-                    for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, c, i >> 2), q + i);
-#pragma unroll
-                    for (int i = 0; i < V; ++i) {
-                        const float df = __fsub_rn(q[i], x[i]);
-                        acc[j] = __fadd_rn(acc[j], __fmul_rn(df, df));
-                    }
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int h = S / 2; h > 0; h >>= 1)
-#pragma unroll
-        for (int j = 0; j < h; ++j) acc[j] = __fadd_rn(acc[j], acc[j + h]);
-    return acc[0];
-}
-
-// The TEAM-lane distance with the row read straight from global memory: lane
-// tl issues the loads of up to SEG of its chunks (tl, tl + TEAM, ...) at once,
-// then sums them in order; wider rows take several such segments.
+// Chunks in flight per lane.
 #ifndef SWB_LDG_SEG
 #define SWB_LDG_SEG 4
 #endif
@@ -321,6 +251,9 @@ __device__ __forceinline__ uint4 ld_row16(const uint4* p) {
     return v;
 }
 
+// Lane tl's partial sum of the row, read straight from global memory: the
+// loads of up to SEG of its chunks (tl, tl + TEAM, ...) go out at once, then
+// the chunks are summed in order; wider rows take several such segments.
 template <int TEAM, typename XT>
 __device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, const XT* __restrict__ grow,
                                                   int dim, int metric, int tl) {
@@ -340,30 +273,31 @@ __device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, 
         for (int u = 0; u < SEG; ++u) {
             const int c = s0 + u * TEAM;
             if (c < nch) {
-                float x[V], q[V];
+                float x[V];
                 widen_u4<XT>(raw[u], x);
 #pragma unroll
-                for (int i = 0; i < V; i += 4) widen16(QLay<XT>::part(sq, dim, c, i >> 2), q + i);
-                if (metric == METRIC_IP) {
-#pragma unroll
-                    for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], x[i]));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < V; ++i) {
-                        const float df = __fsub_rn(q[i], x[i]);
-                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                for (int h = 0; h < V / 4; ++h) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(QLay<XT>::part(sq, dim, c, h));
+                    const float2 q01 = make_float2(q4.x, q4.y), q23 = make_float2(q4.z, q4.w);
+                    const float2 x01 = make_float2(x[4 * h], x[4 * h + 1]);
+                    const float2 x23 = make_float2(x[4 * h + 2], x[4 * h + 3]);
+                    float2 p01, p23;
+                    if (metric == METRIC_IP) {
+                        p01 = f2_mul(q01, x01);
+                        p23 = f2_mul(q23, x23);
+                    } else {
+                        const float2 d01 = f2_sub(q01, x01), d23 = f2_sub(q23, x23);
+                        p01 = f2_mul(d01, d01);
+                        p23 = f2_mul(d23, d23);
                     }
+                    acc = __fadd_rn(acc, p01.x);
+                    acc = __fadd_rn(acc, p01.y);
+                    acc = __fadd_rn(acc, p23.x);
+                    acc = __fadd_rn(acc, p23.y);
                 }
             }
         }
     }
-    return acc;
-}
-
-template <int TP>
-__device__ __forceinline__ float split_reduce(float acc) {
-#pragma unroll
-    for (int off = TP / 2; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(FULL, acc, off, TP));
     return acc;
 }
 

@@ -8,9 +8,8 @@
 //    compaction, sorting and the queue merge are warp-synchronous (ballots and
 //    shuffles, no __syncthreads), and all D neighbours of an expansion probe the
 //    shared table at once, one lane per neighbour;
-//  * neighbour rows are gathered by bulk copies (cp.async.bulk) into a per-warp
-//    ring of shared-memory rows, so a warp has several whole rows in flight
-//    while its teams reduce the ones that have landed;
+//  * neighbour rows are read straight from HBM into registers in 16-byte
+//    chunks, one team of lanes per row; other warps of the SM hide the latency;
 //  * the per-query distance table packs (id + 1, distance bits) into one
 //    64-bit word: one compare-and-swap claims a node or returns its distance;
 //  * Index.search runs as one fused kernel: init, the walk for the whole
@@ -65,8 +64,7 @@ struct Knobs {
     int32_t* qdone;
     int32_t* out_ids;
     float* out_dist;
-    int W, R, warp_bytes, q_shared, cmax;
-    int loader;   // 0: bulk copies into a shared-memory ring; 1: direct loads
+    int W, warp_bytes, q_shared, cmax;
     // sign-code prefilter (advance only; null = off): codes [n][cwords] bits
     // around the corpus mean cmu [dim], per-node scale calpha [n], margin
     const int32_t* codes;
@@ -91,18 +89,16 @@ struct Ctr {
 };
 
 struct Layout {
-    int q, ring, mbar, s_id, s_d, s_e, s_l, n_id, n_d, n_e, n_l, c_id, c_d, c_l, w_v, w_slot, w_d, w_aux,
+    int q, s_id, s_d, s_e, s_l, n_id, n_d, n_e, n_l, c_id, c_d, c_l, w_v, w_slot, w_d, w_aux,
         retired, total;
 };
 
 // q_bytes = 0 when the query lives once per CTA rather than per warp; cmax
 // (a power of two >= 32) bounds the candidates, seeds and rows of one step
-__host__ __device__ inline Layout warp_layout(int L, int R, int rowbytes, int q_bytes, int cmax) {
+__host__ __device__ inline Layout warp_layout(int L, int q_bytes, int cmax) {
     Layout w;
     int o = 0;
-    w.ring = o; o += R * rowbytes;      // 16-byte multiples: first, so rows stay aligned
     w.q = o; o += align16(q_bytes);
-    w.mbar = o; o += align16(R * 8);
     w.s_id = o; o += align16(L * 4);
     w.s_d = o; o += align16(L * 4);
     w.n_id = o; o += align16(L * 4);
@@ -125,8 +121,6 @@ __host__ __device__ inline Layout warp_layout(int L, int R, int rowbytes, int q_
 
 struct WarpMem {
     float* q;
-    char* ring;
-    uint64_t* mbar;
     int* s_id;
     float* s_d;
     uint8_t* s_e;
@@ -147,9 +141,7 @@ struct WarpMem {
 
 __device__ inline WarpMem carve(char* base, const Layout& l) {
     WarpMem w;
-    w.ring = base + l.ring;
     w.q = reinterpret_cast<float*>(base + l.q);
-    w.mbar = reinterpret_cast<uint64_t*>(base + l.mbar);
     w.s_id = reinterpret_cast<int*>(base + l.s_id);
     w.s_d = reinterpret_cast<float*>(base + l.s_d);
     w.n_id = reinterpret_cast<int*>(base + l.n_id);
@@ -229,92 +221,13 @@ __device__ __forceinline__ uint64_t cache_pack(int v, float d) {
 // ---------------------------------------------------------------------------
 // distances for a list of rows: w.w_v[0..m) -> w.w_d[0..m)
 
-struct Ring {
-    uint32_t phases;   // parity of the next wait, one bit per slot
-};
-
-template <typename XT>
-__device__ __forceinline__ void issue_row(const Knobs& K, const WarpMem& w, int item) {
-    const int s = item % K.R;
-    const int v = w.w_v[item];
-    const char* src = reinterpret_cast<const char*>(K.X) + (size_t)v * (size_t)K.rowbytes;
-    fence_proxy_async_smem();
-    mbar_expect_tx(&w.mbar[s], (uint32_t)K.rowbytes);
-    bulk_g2s(w.ring + (size_t)s * K.rowbytes, src, (uint32_t)K.rowbytes, &w.mbar[s]);
-}
-
-// Scores the m rows listed in w.w_v, 32/TP rows at a time (each row on TP
-// lanes carrying one TEAM-lane team, common.cuh), while later rows stream into
-// the ring.  Rows with w.w_slot >= 0 are published to the per-query table
-// `ctab` as soon as they are scored.  Returns false (after draining the copies
-// in flight) if a wait ran out.
-template <int TEAM, int TP, typename XT>
-__device__ bool score_rows(const Knobs& K, const WarpMem& w, int m, Ring& ring, const float* sq,
-                           uint64_t* ctab, int lane) {
-    if (m == 0) return true;
-    constexpr int RPR = 32 / TP;   // rows per round
-    const int R = K.R;             // >= RPR
-    const int grp = lane / TP, p = lane % TP;
-    const int first = m < R ? m : R;
-    if (lane < first) issue_row<XT>(K, w, lane);
-    // Items [base, min(m, base + R)) are in flight at the top of each round,
-    // one per slot.
-    for (int base = 0; base < m; base += RPR) {
-        const int i = base + grp;
-        float acc = 0.f;
-        bool good = true;
-        if (i < m) {
-            const int s = i % R;
-            good = mbar_wait(&w.mbar[s], (ring.phases >> s) & 1u);
-            if (good)
-                acc = split_partial<TEAM, TP, XT>(
-                    sq, reinterpret_cast<const XT*>(w.ring + (size_t)s * K.rowbytes), K.dim, K.metric, p);
-        }
-        acc = split_reduce<TP>(acc);
-        if (p == 0 && i < m && good) {
-            const float d = (K.metric == METRIC_IP) ? __fsub_rn(1.f, acc) : acc;
-            w.w_d[i] = d;
-            const int slot = w.w_slot[i];
-            if (slot >= 0) st_volatile_u64(&ctab[slot], cache_pack(w.w_v[i], d));
-        }
-        // a slot's parity advances only when its wait succeeded
-        const unsigned goodmask = __ballot_sync(FULL, good);
-#pragma unroll
-        for (int t = 0; t < RPR; ++t) {
-            const int ii = base + t;
-            if (ii < m && ((goodmask >> (t * TP)) & 1u)) ring.phases ^= 1u << (ii % R);
-        }
-        if (goodmask != FULL) {
-            // A wait ran out.  Record it, then wait (bounded) for every copy
-            // still in flight before the shared memory can be released.
-            const int end = min(m, base + R);
-            for (int ii = base; ii < end; ++ii) {
-                const int t = ii - base;
-                if (t < RPR && ((goodmask >> (t * TP)) & 1u)) continue;
-                const int s = ii % R;
-                if (lane == 0) mbar_wait(&w.mbar[s], (ring.phases >> s) & 1u);
-                ring.phases ^= 1u << s;
-            }
-            if (lane == 0 && K.status) atomicExch(K.status, ERR_TIMEOUT);
-            __syncwarp();
-            return false;
-        }
-        __syncwarp();
-        if (lane < RPR) {
-            const int ni = base + lane + R;
-            if (ni < m) issue_row<XT>(K, w, ni);
-        }
-    }
-    __syncwarp();
-    return true;
-}
-
-// The direct-load scorer: 32/TEAM rows per round, each team reading its row
-// from global memory into registers (common.cuh team_partial_ldg).  No ring,
-// no barriers; latency is hidden by the other warps of the SM.
+// Scores the m rows listed in w.w_v into w.w_d, 32/TEAM rows per round: each
+// team reads its row from global memory into registers (common.cuh
+// team_partial_ldg); the latency is hidden by the other warps of the SM.  Rows
+// with w.w_slot >= 0 are published to the per-query table `ctab` as soon as
+// they are scored.
 template <int TEAM, typename XT>
-__device__ bool score_rows_ldg(const Knobs& K, const WarpMem& w, int m, const float* sq, uint64_t* ctab,
-                               int lane) {
+__device__ void score_rows(const Knobs& K, const WarpMem& w, int m, const float* sq, uint64_t* ctab, int lane) {
     constexpr int P = 32 / TEAM;
     const int team = lane / TEAM, tl = lane % TEAM;
     const XT* X = reinterpret_cast<const XT*>(K.X);
@@ -331,7 +244,6 @@ __device__ bool score_rows_ldg(const Knobs& K, const WarpMem& w, int m, const fl
         }
     }
     __syncwarp();
-    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -466,9 +378,8 @@ __device__ __forceinline__ void swap_queue(WarpMem& w) {
 
 // Seeds -> sorted queue (local_search.cu:318-350).  Duplicate seeds keep their
 // first occurrence (the CPU reference's rule, _refcpu.py:68-74).
-template <int TEAM, int TP, typename XT>
-__device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring,
-                            Ctr& ctr) {
+template <int TEAM, typename XT>
+__device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ctr& ctr) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     if (vis) {
         if (K.H >= 128) {
@@ -508,8 +419,7 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
     }
     for (int off = 16; off > 0; off >>= 1) fails += __shfl_xor_sync(FULL, fails, off);
     __syncwarp();
-    if (K.loader) score_rows_ldg<TEAM, XT>(K, w, m, sq, nullptr, lane);
-    else score_rows<TEAM, TP, XT>(K, w, m, ring, sq, nullptr, lane);
+    score_rows<TEAM, XT>(K, w, m, sq, nullptr, lane);
     ctr.add(lane, 1, m);
     ctr.add(lane, 2, fails);
     for (int t = lane; t < m; t += 32) {
@@ -613,9 +523,8 @@ __device__ int code_filter(const Knobs& K, const WarpMem& w, int m, const float*
 
 // CODES: compiled with the sign-code prefilter (the advance kernel, when
 // codes are given); the fused search never uses it.
-template <int TEAM, int TP, typename XT, bool CODES = false>
-__device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ring& ring, Ctr& ctr,
-                     int delta) {
+template <int TEAM, typename XT, bool CODES = false>
+__device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ctr& ctr, int delta) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     uint64_t* ctab = (K.Hc > 0) ? K.cache + (size_t)q * (size_t)K.Hc : nullptr;
     float* bnd = K.bound ? K.bound + q : nullptr;
@@ -752,9 +661,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             for (int b = 0; b < m; b += 32)
                 claimed_rows += __popc(__ballot_sync(FULL, b + lane < m && w.w_slot[b + lane] >= 0));
         }
-        const bool scored = K.loader ? score_rows_ldg<TEAM, XT>(K, w, m, sq, ctab, lane)
-                                     : score_rows<TEAM, TP, XT>(K, w, m, ring, sq, ctab, lane);
-        if (!scored) break;
+        score_rows<TEAM, XT>(K, w, m, sq, ctab, lane);
         for (int b = 0; b < m; b += 32) {
             const int i = b + lane;
             const float d = (i < m) ? w.w_d[i] : FLT_MAX;
@@ -834,16 +741,6 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
 // ---------------------------------------------------------------------------
 // per-warp set-up and state transfer
 
-__device__ __forceinline__ void ring_setup(const Knobs& K, WarpMem& w, int lane, Ring& ring) {
-    if (lane == 0 && K.R > 0) {
-        for (int s = 0; s < K.R; ++s) mbar_init(&w.mbar[s], 1);
-        fence_mbar_init();
-        fence_proxy_async_smem();
-    }
-    ring.phases = 0u;
-    __syncwarp();
-}
-
 // the query into shared memory, in the layout QLay<XT> describes
 template <typename XT>
 __device__ __forceinline__ void load_query(float* sq, const float* src, int dim, int tid, int nthreads) {
@@ -881,17 +778,15 @@ __device__ void store_state(const Knobs& K, const WarpMem& w, size_t bid, int la
 // ---------------------------------------------------------------------------
 // kernels
 
-template <int TEAM, int TP, typename XT>
+template <int TEAM, typename XT>
 __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = blockIdx.x * K.W + warp;
     if (g >= K.Q * K.J) return;
     const int q = g / K.J, j = g % K.J;
-    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4, K.cmax);
+    const Layout lay = warp_layout(K.L, K.dim * 4, K.cmax);
     WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
-    Ring ring;
-    ring_setup(K, w, lane, ring);
     load_query<XT>(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
     // the per-query table and bound belong to the query; its J branches clear
     // them between them (local_search.cu:302-313)
@@ -904,11 +799,11 @@ __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs
     if (K.bound && j == 0 && lane == 0) K.bound[q] = FLT_MAX;
     __syncwarp();
     Ctr ctr;
-    init_branch<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr);
+    init_branch<TEAM, XT>(K, w, q, j, lane, w.q, ctr);
     store_state(K, w, (size_t)q * K.J + j, lane, ctr);
 }
 
-template <int TEAM, int TP, typename XT>
+template <int TEAM, typename XT>
 __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -922,17 +817,15 @@ __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Kn
         flat = g;
     }
     const int q = flat / K.J, j = flat % K.J;
-    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, K.dim * 4, K.cmax);
+    const Layout lay = warp_layout(K.L, K.dim * 4, K.cmax);
     WarpMem w = carve(smem + (size_t)warp * K.warp_bytes, lay);
-    Ring ring;
-    ring_setup(K, w, lane, ring);
     load_query<XT>(w.q, K.Qv + (size_t)q * K.dim, K.dim, lane, 32);
     Ctr ctr;
     load_state(K, w, (size_t)flat, lane, ctr);
     if (K.codes)
-        walk<TEAM, TP, XT, true>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
+        walk<TEAM, XT, true>(K, w, q, j, lane, w.q, ctr, K.delta);
     else
-        walk<TEAM, TP, XT>(K, w, q, j, lane, w.q, ring, ctr, K.delta);
+        walk<TEAM, XT>(K, w, q, j, lane, w.q, ctr, K.delta);
     __syncwarp();
     store_state(K, w, (size_t)flat, lane, ctr);
 }
@@ -986,7 +879,7 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
 #ifndef SWB_FUSED_MINB
 #define SWB_FUSED_MINB 5
 #endif
-template <int TEAM, int TP, typename XT>
+template <int TEAM, typename XT>
 __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -997,13 +890,11 @@ __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid
     load_query<XT>(sq, K.Qv + (size_t)q * K.dim, K.dim, threadIdx.x, blockDim.x);
     __syncthreads();
     if (j >= K.J) return;
-    const Layout lay = warp_layout(K.L, K.R, K.rowbytes, 0, K.cmax);
+    const Layout lay = warp_layout(K.L, 0, K.cmax);
     WarpMem w = carve(smem + qbytes + (size_t)warp * K.warp_bytes, lay);
-    Ring ring;
-    ring_setup(K, w, lane, ring);
     Ctr ctr;
-    init_branch<TEAM, TP, XT>(K, w, q, j, lane, sq, ring, ctr);
-    walk<TEAM, TP, XT>(K, w, q, j, lane, sq, ring, ctr, K.max_exp);
+    init_branch<TEAM, XT>(K, w, q, j, lane, sq, ctr);
+    walk<TEAM, XT>(K, w, q, j, lane, sq, ctr, K.max_exp);
     __syncwarp();
     const size_t bid = (size_t)q * K.J + j;
     store_state(K, w, bid, lane, ctr);
@@ -1096,29 +987,6 @@ namespace {
 
 int esize_of(int x_dtype) { return x_dtype == 0 ? 4 : 2; }
 
-// Physical lanes per row (common.cuh split_partial).  TP = TEAM runs one add
-// chain per lane and 32/TEAM rows per round; TP = 4 or 8 runs TEAM/TP chains
-// per lane and 8 or 4 rows per round, which needs a proportionally deeper ring
-// to keep copies overlapping.  SWB_TP overrides.
-int pick_tp(int rowbytes, int team) {
-    (void)rowbytes;
-    int tp = abi::env_int("SWB_TP", team);
-    if (tp != 4 && tp != 8 && tp != 16 && tp != 32) tp = team;
-    if (tp > team) tp = team;
-    return tp;
-}
-
-// Rows in flight per warp: a staging budget per warp, at least one round's
-// rows (32 / tp), at most 32 (one issuing lane each).
-int pick_ring(int rowbytes, int tp) {
-    const int budget = abi::env_int("SWB_RING_BYTES", 12 * 1024);
-    int r = budget / rowbytes;
-    const int rpr = 32 / tp;
-    if (r < rpr) r = rpr;
-    if (r > 32) r = 32;
-    return r;
-}
-
 int pow2_at_least(int x) {
     int p = 1;
     while (p < x) p <<= 1;
@@ -1157,27 +1025,25 @@ int launch(KernelT kern, dim3 grid, int threads, size_t smem, cudaStream_t st, c
     return abi::cuda_check("search kernel launch");
 }
 
-#define SWB_CASE(KERNEL, T, P, TEAMV, TPV, DT, ...)                                           \
-    if ((TEAMV) == T && (TPV) == P)                                                            \
-        return ((DT) == SWB_F32) ? launch(KERNEL<T, P, float>, __VA_ARGS__)                    \
-                                 : launch(KERNEL<T, P, __half>, __VA_ARGS__);
-#define SWB_DISPATCH(KERNEL, TEAMV, TPV, DT, ...)                                              \
+// the query's shared-memory bytes (common.cuh QLay)
+int query_bytes(int dim) { return align16(4 * dim); }
+
+#define SWB_CASE(KERNEL, T, TEAMV, DT, ...)                                                    \
+    if ((TEAMV) == T)                                                                          \
+        return ((DT) == SWB_F32) ? launch(KERNEL<T, float>, __VA_ARGS__)                       \
+                                 : launch(KERNEL<T, __half>, __VA_ARGS__);
+#define SWB_DISPATCH(KERNEL, TEAMV, DT, ...)                                                   \
     [&]() -> int {                                                                             \
-        SWB_CASE(KERNEL, 4, 4, TEAMV, TPV, DT, __VA_ARGS__)                                    \
-        SWB_CASE(KERNEL, 8, 4, TEAMV, TPV, DT, __VA_ARGS__)                                    \
-        SWB_CASE(KERNEL, 8, 8, TEAMV, TPV, DT, __VA_ARGS__)                                    \
-        SWB_CASE(KERNEL, 16, 4, TEAMV, TPV, DT, __VA_ARGS__)                                   \
-        SWB_CASE(KERNEL, 16, 8, TEAMV, TPV, DT, __VA_ARGS__)                                   \
-        SWB_CASE(KERNEL, 16, 16, TEAMV, TPV, DT, __VA_ARGS__)                                  \
-        SWB_CASE(KERNEL, 32, 4, TEAMV, TPV, DT, __VA_ARGS__)                                   \
-        SWB_CASE(KERNEL, 32, 8, TEAMV, TPV, DT, __VA_ARGS__)                                   \
-        SWB_CASE(KERNEL, 32, 32, TEAMV, TPV, DT, __VA_ARGS__)                                  \
+        SWB_CASE(KERNEL, 4, TEAMV, DT, __VA_ARGS__)                                            \
+        SWB_CASE(KERNEL, 8, TEAMV, DT, __VA_ARGS__)                                            \
+        SWB_CASE(KERNEL, 16, TEAMV, DT, __VA_ARGS__)                                           \
+        SWB_CASE(KERNEL, 32, TEAMV, DT, __VA_ARGS__)                                           \
         return abi::fail(SWB_ERR_TEAM, "team_size must be 4, 8, 16 or 32");                   \
     }()
 
 // cmax bounds what one step handles: D candidates, V seeds, and (fused) the
 // J branch heads of the final merge, which reuse 4 * cmax ints
-int fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int team, int L, bool q_shared, int D,
+void fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int team, int L, bool q_shared, int D,
                 int V, int J) {
     std::memset(&K, 0, sizeof(K));
     K.X = X;
@@ -1185,19 +1051,15 @@ int fill_common(Knobs& K, const void* X, int x_dtype, int64_t n, int dim, int te
     K.dim = dim;
     K.rowbytes = dim * esize_of(x_dtype);
     K.L = L;
-    const int tp = pick_tp(K.rowbytes, team);
-    K.loader = abi::env_int("SWB_LOADER", 1) ? 1 : 0;
     K.codes = nullptr; K.calpha = nullptr; K.cmu = nullptr; K.cmargin = 0.f; K.cwords = 0;
-    K.R = K.loader ? 0 : pick_ring(K.rowbytes, tp);
     K.q_shared = q_shared ? 1 : 0;
     int cm = pow2_at_least(D > V ? D : V);
     const int jq = (J + 3) / 4;
     if (cm < jq) cm = pow2_at_least(jq);
     if (cm < 32) cm = 32;
     K.cmax = cm;
-    const Layout lay = warp_layout(L, K.R, K.rowbytes, q_shared ? 0 : dim * 4, cm);
+    const Layout lay = warp_layout(L, q_shared ? 0 : query_bytes(dim), cm);
     K.warp_bytes = lay.total;
-    return tp;
 }
 
 }  // namespace
@@ -1218,7 +1080,7 @@ extern "C" int swb_search_init(const void* X, int x_dtype, int64_t n, int dim, c
     if (!Qv || !seeds || !ids || !dist || !expanded || !lineage || !counters || (H > 1 && !visited))
         return abi::fail(SWB_ERR_ARG, "null state buffer");
     Knobs K;
-    const int tp = fill_common(K, X, x_dtype, n, dim, team, L, false, 1, V, 0);
+    fill_common(K, X, x_dtype, n, dim, team, L, false, 1, V, 0);
     K.Qv = Qv; K.seeds = seeds; K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
     K.metric = metric; K.cache = Hc > 0 ? cache : nullptr; K.Hc = Hc > 0 ? Hc : 0; K.bound = bound;
@@ -1226,7 +1088,7 @@ extern "C" int swb_search_init(const void* X, int x_dtype, int64_t n, int dim, c
     const long long warps = (long long)Q * J;
     dim3 grid((unsigned)((warps + K.W - 1) / K.W));
     const size_t smem = (size_t)K.W * K.warp_bytes;
-    return SWB_DISPATCH(init_kernel, team, tp, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH(init_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim, const int32_t* G, int D,
@@ -1251,7 +1113,7 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     if (Q <= 0 || J <= 0 || delta <= 0) return SWB_OK;
     if (active && n_active <= 0) return SWB_OK;
     Knobs K;
-    const int tp = fill_common(K, X, x_dtype, n, dim, team, L, false, D, 1, 0);
+    fill_common(K, X, x_dtype, n, dim, team, L, false, D, 1, 0);
     K.G = G; K.D = D; K.Qv = Qv; K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V < 1 ? 1 : V; K.visited = visited; K.H = H; K.counters = counters;
     K.metric = metric; K.delta = delta; K.max_exp = max_expansions; K.policy = policy;
@@ -1266,7 +1128,7 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     const long long warps = active ? (long long)n_active : (long long)Q * J;
     dim3 grid((unsigned)((warps + K.W - 1) / K.W));
     const size_t smem = (size_t)K.W * K.warp_bytes;
-    return SWB_DISPATCH(advance_kernel, team, tp, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH(advance_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int32_t* qdone, void* stream) {
@@ -1305,7 +1167,7 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
         return abi::fail(SWB_ERR_ARG, "state outputs must be all given or all null");
     Knobs K;
     if (J > 4 * MAXD) return abi::fail(SWB_ERR_ARG, "at most %d branches per query", 4 * MAXD);
-    const int tp = fill_common(K, X, x_dtype, n, dim, team, L, true, D, V, J);
+    fill_common(K, X, x_dtype, n, dim, team, L, true, D, V, J);
     K.G = G; K.D = D; K.Qv = Qv; K.seeds = seeds;
     K.ids = ids; K.dist = dist; K.expd = expanded; K.lin = lineage;
     K.Q = Q; K.J = J; K.V = V; K.visited = visited; K.H = H; K.counters = counters;
@@ -1322,8 +1184,8 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     if (W > 8) W = 8;
     K.W = W;
     dim3 grid((unsigned)((J + W - 1) / W), (unsigned)Q);
-    const size_t smem = (size_t)align16(dim * 4) + (size_t)W * K.warp_bytes;
-    return SWB_DISPATCH(fused_kernel, team, tp, x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
+    const size_t smem = (size_t)query_bytes(dim) + (size_t)W * K.warp_bytes;
+    return SWB_DISPATCH(fused_kernel, team, x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_merge_branches(const int32_t* bids, const float* bdist, int Q, int J, int kk, int k,
