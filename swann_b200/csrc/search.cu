@@ -523,7 +523,9 @@ __device__ int code_filter(const Knobs& K, const WarpMem& w, int m, const float*
 
 // CODES: compiled with the sign-code prefilter (the advance kernel, when
 // codes are given); the fused search never uses it.
-template <int TEAM, typename XT, bool CODES = false>
+// NT: neighbour slots per lane (the graph degree is at most 32 * NT); 2 for
+// degree <= 64 keeps half the per-neighbour registers of 4.
+template <int TEAM, typename XT, int NT, bool CODES = false>
 __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ctr& ctr, int delta) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     uint64_t* ctab = (K.Hc > 0) ? K.cache + (size_t)q * (size_t)K.Hc : nullptr;
@@ -561,12 +563,12 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
         ctr.expand();
 
         // -- expand p: one lane per neighbour slot ------------------------
-        int nv[4], nst[4], nsl[4];
-        float nd[4];
+        int nv[NT], nst[NT], nsl[NT];
+        float nd[NT];
         int cov = 0, nbr = 0, fails = 0, hits = 0;
-        bool fresh[4];   // passed the visited table; to be probed in the query's table
+        bool fresh[NT];   // passed the visited table; to be probed in the query's table
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < NT; ++t) {
             const int nidx = lane + 32 * t;
             int v = (nidx < D) ? __ldg(&K.G[(size_t)p * D + nidx]) : -1;
             if (v >= K.n) v = -1;   // an edge outside the corpus is no edge
@@ -577,7 +579,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             fresh[t] = false;
         }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < NT; ++t) {
             const int v = nv[t];
             if (v < 0) continue;
             ++nbr;
@@ -589,12 +591,12 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
         }
         // The first probe of every fresh neighbour goes out at once (one
         // compare-and-swap each, independent); only collisions probe on.
-        unsigned long long first_old[4];
-        uint32_t first_pos[4];
+        unsigned long long first_old[NT];
+        uint32_t first_pos[NT];
         if (ctab) {
             const uint32_t cmask = (uint32_t)(K.Hc - 1);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
+            for (int t = 0; t < NT; ++t) {
                 if (!fresh[t]) continue;
                 const uint32_t key = (uint32_t)(nv[t] + 1);
                 first_pos[t] = knuth(nv[t], cmask);
@@ -603,7 +605,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             }
         }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < NT; ++t) {
             if (!fresh[t]) continue;
             const int v = nv[t];
             int cslot = -1, claimed = 0;
@@ -634,7 +636,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
         const float worst = (w.s_id[L - 1] >= 0) ? w.s_d[L - 1] : FLT_MAX;
         int m = 0, nk = 0, claimed_rows = 0;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < NT; ++t) {
             const unsigned msk = __ballot_sync(FULL, nst[t] == 2);
             if (nst[t] == 2) {
                 const int ps = m + __popc(msk & lanemask_lt());
@@ -803,7 +805,7 @@ __global__ void __launch_bounds__(256) init_kernel(const __grid_constant__ Knobs
     store_state(K, w, (size_t)q * K.J + j, lane, ctr);
 }
 
-template <int TEAM, typename XT>
+template <int TEAM, typename XT, int NT>
 __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -823,9 +825,9 @@ __global__ void __launch_bounds__(256) advance_kernel(const __grid_constant__ Kn
     Ctr ctr;
     load_state(K, w, (size_t)flat, lane, ctr);
     if (K.codes)
-        walk<TEAM, XT, true>(K, w, q, j, lane, w.q, ctr, K.delta);
+        walk<TEAM, XT, NT, true>(K, w, q, j, lane, w.q, ctr, K.delta);
     else
-        walk<TEAM, XT>(K, w, q, j, lane, w.q, ctr, K.delta);
+        walk<TEAM, XT, NT>(K, w, q, j, lane, w.q, ctr, K.delta);
     __syncwarp();
     store_state(K, w, (size_t)flat, lane, ctr);
 }
@@ -879,7 +881,7 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
 #ifndef SWB_FUSED_MINB
 #define SWB_FUSED_MINB 5
 #endif
-template <int TEAM, typename XT>
+template <int TEAM, typename XT, int NT>
 __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -894,7 +896,7 @@ __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid
     WarpMem w = carve(smem + qbytes + (size_t)warp * K.warp_bytes, lay);
     Ctr ctr;
     init_branch<TEAM, XT>(K, w, q, j, lane, sq, ctr);
-    walk<TEAM, XT>(K, w, q, j, lane, sq, ctr, K.max_exp);
+    walk<TEAM, XT, NT>(K, w, q, j, lane, sq, ctr, K.max_exp);
     __syncwarp();
     const size_t bid = (size_t)q * K.J + j;
     store_state(K, w, bid, lane, ctr);
@@ -1028,6 +1030,9 @@ int launch(KernelT kern, dim3 grid, int threads, size_t smem, cudaStream_t st, c
 // the query's shared-memory bytes (common.cuh QLay)
 int query_bytes(int dim) { return align16(4 * dim); }
 
+// neighbour slots per lane for a graph of degree D (walk's NT)
+int slots_for(int D) { return D <= 64 ? 2 : 4; }
+
 #define SWB_CASE(KERNEL, T, TEAMV, DT, ...)                                                    \
     if ((TEAMV) == T)                                                                          \
         return ((DT) == SWB_F32) ? launch(KERNEL<T, float>, __VA_ARGS__)                       \
@@ -1040,6 +1045,23 @@ int query_bytes(int dim) { return align16(4 * dim); }
         SWB_CASE(KERNEL, 32, TEAMV, DT, __VA_ARGS__)                                           \
         return abi::fail(SWB_ERR_TEAM, "team_size must be 4, 8, 16 or 32");                   \
     }()
+#define SWB_CASE_NT(KERNEL, T, N, TEAMV, NTV, DT, ...)                                         \
+    if ((TEAMV) == T && (NTV) == N)                                                            \
+        return ((DT) == SWB_F32) ? launch(KERNEL<T, float, N>, __VA_ARGS__)                    \
+                                 : launch(KERNEL<T, __half, N>, __VA_ARGS__);
+#define SWB_DISPATCH_NT(KERNEL, TEAMV, NTV, DT, ...)                                           \
+    [&]() -> int {                                                                             \
+        SWB_CASE_NT(KERNEL, 4, 2, TEAMV, NTV, DT, __VA_ARGS__)                                 \
+        SWB_CASE_NT(KERNEL, 4, 4, TEAMV, NTV, DT, __VA_ARGS__)                                 \
+        SWB_CASE_NT(KERNEL, 8, 2, TEAMV, NTV, DT, __VA_ARGS__)                                 \
+        SWB_CASE_NT(KERNEL, 8, 4, TEAMV, NTV, DT, __VA_ARGS__)                                 \
+        SWB_CASE_NT(KERNEL, 16, 2, TEAMV, NTV, DT, __VA_ARGS__)                                \
+        SWB_CASE_NT(KERNEL, 16, 4, TEAMV, NTV, DT, __VA_ARGS__)                                \
+        SWB_CASE_NT(KERNEL, 32, 2, TEAMV, NTV, DT, __VA_ARGS__)                                \
+        SWB_CASE_NT(KERNEL, 32, 4, TEAMV, NTV, DT, __VA_ARGS__)                                \
+        return abi::fail(SWB_ERR_TEAM, "team_size must be 4, 8, 16 or 32");                   \
+    }()
+
 
 // cmax bounds what one step handles: D candidates, V seeds, and (fused) the
 // J branch heads of the final merge, which reuse 4 * cmax ints
@@ -1128,7 +1150,7 @@ extern "C" int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim
     const long long warps = active ? (long long)n_active : (long long)Q * J;
     dim3 grid((unsigned)((warps + K.W - 1) / K.W));
     const size_t smem = (size_t)K.W * K.warp_bytes;
-    return SWB_DISPATCH(advance_kernel, team, x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH_NT(advance_kernel, team, slots_for(D), x_dtype, grid, K.W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int32_t* qdone, void* stream) {
@@ -1185,7 +1207,7 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.W = W;
     dim3 grid((unsigned)((J + W - 1) / W), (unsigned)Q);
     const size_t smem = (size_t)query_bytes(dim) + (size_t)W * K.warp_bytes;
-    return SWB_DISPATCH(fused_kernel, team, x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
+    return SWB_DISPATCH_NT(fused_kernel, team, slots_for(D), x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
 }
 
 extern "C" int swb_merge_branches(const int32_t* bids, const float* bdist, int Q, int J, int kk, int k,
