@@ -251,6 +251,13 @@ __device__ __forceinline__ uint4 ld_row16(const uint4* p) {
     return v;
 }
 
+// A whole row into L2 with one instruction (16-byte aligned, size a multiple
+// of 16): issued as a team starts a row, it turns the row's later segments
+// into L2 hits instead of dependent DRAM round trips.
+__device__ __forceinline__ void prefetch_row_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Lane tl's partial sum of the row, read straight from global memory: the
 // loads of up to SEG of its chunks (tl, tl + TEAM, ...) go out at once, then
 // the chunks are summed in order; wider rows take several such segments.
