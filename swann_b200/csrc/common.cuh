@@ -235,9 +235,11 @@ __device__ __forceinline__ float team_reduce(float acc) {
     return acc;
 }
 
-// Chunks in flight per lane.
+// Chunks in flight per lane (a segment); a row's later segments are L2 hits
+// after its whole-row prefetch, so short segments cost little and leave
+// registers for occupancy.
 #ifndef SWB_LDG_SEG
-#define SWB_LDG_SEG 4
+#define SWB_LDG_SEG 3
 #endif
 // One 16-byte chunk of a corpus row, read without allocating in L1: a row is
 // read once per query, and L1 is worth more to the spilled registers (2% on

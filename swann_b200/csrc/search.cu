@@ -886,13 +886,14 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
     for (int t = w + lane; t < k; t += 32) { oi[t] = -1; od[t] = __int_as_float(0x7f800000); }
 }
 
-// Register budget of the fused kernel: 65536 / (256 * 5) -> 48 registers a
-// thread, with 4 warps (4 branches) a CTA.  Measured at C3 (1M x 1536 fp16,
-// batch 65535): occupancy buys more than the spills it costs -- 48 registers
-// and 4-chunk segments ran 4% faster than 64 registers and 6-chunk segments,
-// and 80 registers (no spills) ran slowest.
+// Register budget of the fused kernel: 65536 / (256 * 6) -> 40 registers a
+// thread, 12 CTAs of 4 warps (4 branches) an SM.  Measured at C3 (1M x 1536
+// fp16, batch 65535): occupancy buys more than the spills it costs.  With the
+// whole-row L2 prefetch, 40 registers and 3-chunk segments run 767k QPS, 48
+// registers and 4-chunk segments 744-748k, 40 registers and 4-chunk segments
+// 732k, 32 registers 710k; 80 registers (no spills) ran slowest of all.
 #ifndef SWB_FUSED_MINB
-#define SWB_FUSED_MINB 5
+#define SWB_FUSED_MINB 6
 #endif
 template <int TEAM, typename XT, int NT>
 __global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
