@@ -341,6 +341,16 @@ def cpu_baseline(X, G, Q, seeds, cfg, op, budget_s=15.0):
             "seconds": el}
 
 
+# per-query table slots per claim of the busiest query (then a power of two);
+# the clear of the table is a full write of it every step
+TABLE_HEADROOM = 1.5
+
+
+def table_slots_for(claims):
+    from swann_b200 import _engine as E
+    return max(4096, E.next_pow2(int(TABLE_HEADROOM * claims)))
+
+
 def calibrate(index, Qs, truth, cfg):
     """Fastest (branches, queue, stop_eps) with recall >= TARGET on Qs."""
     best = None
@@ -408,9 +418,9 @@ def run(args):
         op = box[0]
 
     # Size the per-query distance table from what the queries actually claim:
-    # twice the busiest query's claims (load <= 50% for that query, a few
-    # percent for a typical one), a power of two.  A probe run that finds no
-    # slot scores the row uncached, so a fuller table costs dedup, not results.
+    # TABLE_HEADROOM times the busiest query's claims, a power of two (load
+    # <= 67% for that query, ~15% for a typical one).  A probe run that finds
+    # no slot scores the row uncached, so a fuller table costs dedup, not results.
     ent = S.select_nearest(Q[:gt_n], index._cat, op["branches"], metric=index._m)
     sd = index.catalogue[ent].to(torch.int32)
     _, _, ctr, _ = E.search_fused_lean(X, G, Q[:gt_n], sd, k=cfg["k"], L=op["queue"], B=64, metric=index._m,
@@ -418,7 +428,7 @@ def run(args):
                                        shared_bound=True, exclusive=2, elide_visited=True)
     claims = (ctr[..., 5].to(torch.int64).sum(1) + op["branches"]).max().item()
     ref_slots = E.cache_size(op["branches"], 64, G.shape[1])
-    slots = min(ref_slots, max(4096, E.next_pow2(2 * int(claims))))
+    slots = min(ref_slots, table_slots_for(claims))
     index.table_slots = slots
     table = {"slots": slots, "reference_slots": ref_slots, "max_claims_per_query": int(claims),
              "max_load": round(claims / slots, 4)}
@@ -718,7 +728,7 @@ def run_batch_sweep(args):
                                            team_size=16, stop_eps=eps, shared_cache=True, shared_bound=True,
                                            exclusive=2, elide_visited=True)
         claims = (ctr[..., 5].to(torch.int64).sum(1) + br).max().item()
-        ops[br] = (eps, r, min(E.cache_size(br, 64, G.shape[1]), max(4096, E.next_pow2(2 * int(claims)))))
+        ops[br] = (eps, r, min(E.cache_size(br, 64, G.shape[1]), table_slots_for(claims)))
     rows = []
     for b, br in BATCH_SWEEP:
         eps, r, slots = ops[br]
