@@ -235,11 +235,11 @@ __device__ __forceinline__ float team_reduce(float acc) {
     return acc;
 }
 
-// Chunks in flight per lane (a segment); a row's later segments are L2 hits
-// after its whole-row prefetch, so short segments cost little and leave
-// registers for occupancy.
+// Chunks of each row in flight per lane (a segment); a row's later segments
+// are L2 hits after its whole-row prefetch, so short segments cost little and
+// leave registers for occupancy.
 #ifndef SWB_LDG_SEG
-#define SWB_LDG_SEG 3
+#define SWB_LDG_SEG 1
 #endif
 // One 16-byte chunk of a corpus row, read without allocating in L1: a row is
 // read once per query, and L1 is worth more to the spilled registers (2% on
@@ -260,54 +260,81 @@ __device__ __forceinline__ void prefetch_row_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Lane tl's partial sum of the row, read straight from global memory: the
-// loads of up to SEG of its chunks (tl, tl + TEAM, ...) go out at once, then
-// the chunks are summed in order; wider rows take several such segments.
-template <int TEAM, typename XT>
-__device__ __forceinline__ float team_partial_ldg(const float* __restrict__ sq, const XT* __restrict__ grow,
-                                                  int dim, int metric, int tl) {
+// Elements 4h .. 4h+3 of a 16-byte chunk held in registers, widened to fp32
+template <typename XT>
+__device__ __forceinline__ void widen_part(const uint4& v, int h, float* out);
+template <>
+__device__ __forceinline__ void widen_part<float>(const uint4& v, int, float* out) {
+    out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+    out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+template <>
+__device__ __forceinline__ void widen_part<__half>(const uint4& v, int h, float* out) {
+    union { uint32_t u; __half2 h2; } c0, c1;
+    c0.u = h ? v.z : v.x;
+    c1.u = h ? v.w : v.y;
+    const float2 f0 = __half22float2(c0.h2), f1 = __half22float2(c1.h2);
+    out[0] = f0.x; out[1] = f0.y; out[2] = f1.x; out[3] = f1.y;
+}
+
+// R rows at once on one team, read straight from global memory: lane tl's
+// partial sum of each row r < nrows into acc[r], every row its own chain in
+// the reference's order (lane tl owns chunks tl, tl + TEAM, ...; within a
+// chunk, elements in order).  The loads of all R rows' segments go out
+// together (the first, DRAM-bound segment of R rows in one round trip) and the
+// R add chains advance in turn, one add each.  Rows r >= nrows are neither
+// read nor meaningful.
+template <int TEAM, typename XT, int R, int SEG>
+__device__ __forceinline__ void team_partial_rows(const float* __restrict__ sq, const XT* const (&rows)[R],
+                                                  int nrows, int dim, int metric, int tl, float (&acc)[R]) {
     constexpr int V = VecN<XT>::N;
-    constexpr int SEG = SWB_LDG_SEG;
-    const uint4* r4 = reinterpret_cast<const uint4*>(grow);
     const int nch = dim / V;
-    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
     for (int s0 = tl; s0 < nch; s0 += TEAM * SEG) {
-        uint4 raw[SEG];
+        uint4 raw[R][SEG];
 #pragma unroll
         for (int u = 0; u < SEG; ++u) {
             const int c = s0 + u * TEAM;
-            raw[u] = (c < nch) ? ld_row16(r4 + c) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                raw[r][u] = (c < nch && r < nrows) ? ld_row16(reinterpret_cast<const uint4*>(rows[r]) + c)
+                                                   : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
         for (int u = 0; u < SEG; ++u) {
             const int c = s0 + u * TEAM;
             if (c < nch) {
-                float x[V];
-                widen_u4<XT>(raw[u], x);
 #pragma unroll
                 for (int h = 0; h < V / 4; ++h) {
                     const float4 q4 = *reinterpret_cast<const float4*>(QLay<XT>::part(sq, dim, c, h));
                     const float2 q01 = make_float2(q4.x, q4.y), q23 = make_float2(q4.z, q4.w);
-                    const float2 x01 = make_float2(x[4 * h], x[4 * h + 1]);
-                    const float2 x23 = make_float2(x[4 * h + 2], x[4 * h + 3]);
-                    float2 p01, p23;
-                    if (metric == METRIC_IP) {
-                        p01 = f2_mul(q01, x01);
-                        p23 = f2_mul(q23, x23);
-                    } else {
-                        const float2 d01 = f2_sub(q01, x01), d23 = f2_sub(q23, x23);
-                        p01 = f2_mul(d01, d01);
-                        p23 = f2_mul(d23, d23);
+                    float p[R][4];
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        float x[4];
+                        widen_part<XT>(raw[r][u], h, x);
+                        const float2 x01 = make_float2(x[0], x[1]), x23 = make_float2(x[2], x[3]);
+                        float2 p01, p23;
+                        if (metric == METRIC_IP) {
+                            p01 = f2_mul(q01, x01);
+                            p23 = f2_mul(q23, x23);
+                        } else {
+                            const float2 d01 = f2_sub(q01, x01), d23 = f2_sub(q23, x23);
+                            p01 = f2_mul(d01, d01);
+                            p23 = f2_mul(d23, d23);
+                        }
+                        p[r][0] = p01.x; p[r][1] = p01.y; p[r][2] = p23.x; p[r][3] = p23.y;
                     }
-                    acc = __fadd_rn(acc, p01.x);
-                    acc = __fadd_rn(acc, p01.y);
-                    acc = __fadd_rn(acc, p23.x);
-                    acc = __fadd_rn(acc, p23.y);
+                    // the rows' chains advance in turn, one add each
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+#pragma unroll
+                        for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], p[r][e]);
                 }
             }
         }
     }
-    return acc;
 }
 
 }  // namespace swb

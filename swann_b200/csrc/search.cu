@@ -226,34 +226,60 @@ __device__ __forceinline__ uint64_t cache_pack(int v, float d) {
 #ifndef SWB_ROW_PREFETCH
 #define SWB_ROW_PREFETCH 1
 #endif
+// Rows per team and round (common.cuh team_partial_rows).  Measured at C3
+// (fp16, d 1536, 40 registers, 1-chunk segments): 2 rows 877-882k QPS against
+// 779-781k for one row at a time; 3 rows 792k and 4 rows 738k (more spills);
+// 2 rows with 2-chunk segments 792k.
+#ifndef SWB_ROWS
+#define SWB_ROWS 2
+#endif
 
-// Scores the m rows listed in w.w_v into w.w_d, 32/TEAM rows per round: each
-// team reads its row from global memory into registers (common.cuh
-// team_partial_ldg); the latency is hidden by the other warps of the SM.  Rows
-// with w.w_slot >= 0 are published to the per-query table `ctab` as soon as
-// they are scored.
+// Scores the m rows listed in w.w_v into w.w_d, SWB_ROWS * 32/TEAM rows per
+// round: each team reads SWB_ROWS rows from global memory into registers and
+// sums them side by side (common.cuh team_partial_rows); the latency is hidden
+// by the other warps of the SM.  Rows with w.w_slot >= 0 are published to the
+// per-query table `ctab` as soon as they are scored.
 template <int TEAM, typename XT>
 __device__ void score_rows(const Knobs& K, const WarpMem& w, int m, const float* sq, uint64_t* ctab, int lane) {
     constexpr int P = 32 / TEAM;
     const int team = lane / TEAM, tl = lane % TEAM;
     const XT* X = reinterpret_cast<const XT*>(K.X);
-    for (int base = 0; base < m; base += P) {
-        const int i = base + team;
-        float acc = 0.f;
-        if (i < m) {
-            const XT* row = X + (size_t)w.w_v[i] * K.dim;
+    constexpr int R = SWB_ROWS;
+    for (int base = 0; base < m; base += R * P) {
+        const int i0 = base + team;
+        float acc[R];
+        const XT* rows[R];
+        int nrows = 0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = i0 + r * P;
+            rows[r] = (i < m) ? X + (size_t)w.w_v[i] * K.dim : X;
+            nrows += (i < m) ? 1 : 0;
+        }
+        if (nrows > 0) {
 #if SWB_ROW_PREFETCH
             // rows longer than one segment: the later segments hit L2
-            if (tl == 0 && K.rowbytes > TEAM * SWB_LDG_SEG * 16) prefetch_row_l2(row, (uint32_t)K.rowbytes);
+            if (K.rowbytes > TEAM * SWB_LDG_SEG * 16 && tl < nrows) {
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (tl == r) prefetch_row_l2(rows[r], (uint32_t)K.rowbytes);
+            }
 #endif
-            acc = team_partial_ldg<TEAM, XT>(sq, row, K.dim, K.metric, tl);
+            team_partial_rows<TEAM, XT, R, SWB_LDG_SEG>(sq, rows, nrows, K.dim, K.metric, tl, acc);
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] = 0.f;
         }
-        acc = team_reduce<TEAM>(acc);
-        if (tl == 0 && i < m) {
-            const float d = (K.metric == METRIC_IP) ? __fsub_rn(1.f, acc) : acc;
-            w.w_d[i] = d;
-            const int slot = w.w_slot[i];
-            if (slot >= 0) st_volatile_u64(&ctab[slot], cache_pack(w.w_v[i], d));
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float sum = team_reduce<TEAM>(acc[r]);
+            const int i = i0 + r * P;
+            if (tl == 0 && i < m) {
+                const float d = (K.metric == METRIC_IP) ? __fsub_rn(1.f, sum) : sum;
+                w.w_d[i] = d;
+                const int slot = w.w_slot[i];
+                if (slot >= 0) st_volatile_u64(&ctab[slot], cache_pack(w.w_v[i], d));
+            }
         }
     }
     __syncwarp();
@@ -889,9 +915,10 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
 // Register budget of the fused kernel: 65536 / (256 * 6) -> 40 registers a
 // thread, 12 CTAs of 4 warps (4 branches) an SM.  Measured at C3 (1M x 1536
 // fp16, batch 65535): occupancy buys more than the spills it costs.  With the
-// whole-row L2 prefetch, 40 registers and 3-chunk segments run 767k QPS, 48
-// registers and 4-chunk segments 744-748k, 40 registers and 4-chunk segments
-// 732k, 32 registers 710k; 80 registers (no spills) ran slowest of all.
+// whole-row L2 prefetch and one row a team, 40 registers and 3-chunk segments
+// ran 767k QPS, 48 registers and 4-chunk segments 744-748k, 40 registers and
+// 4-chunk segments 732k, 32 registers 710k; 80 registers (no spills) ran
+// slowest of all.  Two rows a team: 40 registers 819-856k, 48 registers 852k.
 #ifndef SWB_FUSED_MINB
 #define SWB_FUSED_MINB 6
 #endif
