@@ -539,6 +539,10 @@ def run(args):
     roofline = {"bound": "hbm", "kernel": "swb::fused_kernel", "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                 "traffic": traffic, "traffic_source": traffic_src,
+                # what DRAM itself moved per second (the measured traffic over this run's kernel time); the
+                # algorithmic rate above also counts the rows that L2 serves to queries run side by side
+                "dram_gbs": round(traffic / (fused_ms / 1e3) / 1e9, 1) if traffic else None,
+                "dram_frac": round(traffic / (fused_ms / 1e3) / 1e9 / peak, 4) if traffic else None,
                 "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": round(fused_ms, 3),
                 "prepare_ms": round(prep_ms, 3),
                 "per_query": {"distinct_nodes_scored": nodes / batch, "expansions": exps / batch}}
