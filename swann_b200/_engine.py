@@ -400,8 +400,27 @@ class Workspace:
 _WS = Workspace()
 
 
+def prepare_lean(Q, J, B, D, dev, stream, table_slots=None, shared_cache=True, shared_bound=True):
+    """Clears what a query's branches share -- the per-query tables, bounds and
+    completion counters of the lean workspace -- for a following
+    search_fused_lean(..., prepared=True) of Q queries and J branches, on
+    `stream`, so the clear can run beside other work (the seed selection).  The
+    caller orders that search after this stream's work (an event)."""
+    Hc = table_slots or cache_size(J, B, D)
+    shared = J > 1
+    cache = (_WS.get("cache", Q * Hc, torch.int64, dev).view(Q, -1)
+             if (shared_cache and shared) else _empty(torch.int64, dev, (0, 0)))
+    bound = _WS.get("bound", Q, torch.float32, dev) if (shared_bound and shared) else _empty(torch.float32, dev)
+    qdone = _WS.get("qdone", Q, torch.int32, dev)
+    Hc = cache.shape[1] if cache.numel() else 0
+    with torch.cuda.device(dev):
+        N.check(N.lib().swb_search_prepare(Q, N.ptr(cache), Hc, N.ptr(bound), N.ptr(qdone), stream.cuda_stream),
+                "search")
+
+
 def _fused(X, G, Qv, seeds, k, L, B, metric, team_size, policy, stop_eps, shared_cache, shared_bound,
-           exclusive, stall_patience, crowd_frac, elide_visited, kstop, keep_state, table_slots=None):
+           exclusive, stall_patience, crowd_frac, elide_visited, kstop, keep_state, table_slots=None,
+           prepared=False):
     _check_inputs(X, Qv)
     if not (G.is_cuda and G.dtype == torch.int32 and G.is_contiguous()):
         raise ValueError("G: contiguous cuda int32")
@@ -436,7 +455,8 @@ def _fused(X, G, Qv, seeds, k, L, B, metric, team_size, policy, stop_eps, shared
     lib = N.lib()
     with torch.cuda.device(dev):
         s = N.stream_of(X)
-        N.check(lib.swb_search_prepare(Q, N.ptr(cache), Hc, N.ptr(bound), N.ptr(qdone), s), "search")
+        if not prepared:
+            N.check(lib.swb_search_prepare(Q, N.ptr(cache), Hc, N.ptr(bound), N.ptr(qdone), s), "search")
         rc = lib.swb_search_fused(
             N.ptr(X), N.dtype_code(X), X.shape[0], X.shape[1], N.ptr(G), D, N.ptr(Qv), N.ptr(seeds),
             Q, J, V, k, L, B, int(metric), int(team_size), int(policy), float(stop_eps), int(kstop),
@@ -462,13 +482,15 @@ def search_fused(X, G, Qv, seeds, k=10, L=16, B=16, metric=METRIC_IP, team_size=
 
 def search_fused_lean(X, G, Qv, seeds, k=10, L=16, B=16, metric=METRIC_IP, team_size=32, policy=POLICY_BEST,
                       stop_eps=-1.0, shared_cache=False, shared_bound=False, exclusive=False, stall_patience=0,
-                      crowd_frac=0.0, elide_visited=False, kstop=None, table_slots=None):
+                      crowd_frac=0.0, elide_visited=False, kstop=None, table_slots=None, prepared=False):
     """The fused search writing only results, counters [Q, J, NCTR] and the
     status word (the path Index.search runs).  `table_slots` overrides the
-    per-query table size (a power of two).  Returns (ids, dist, ctr, status)."""
+    per-query table size (a power of two); `prepared`: the shared state was
+    already cleared by prepare_lean (same Q, J, B, D, table_slots), ordered
+    before this call.  Returns (ids, dist, ctr, status)."""
     oi, od, _, ctr, status = _fused(X, G, Qv, seeds, k, L, B, metric, team_size, policy, stop_eps, shared_cache,
                                     shared_bound, exclusive, stall_patience, crowd_frac, elide_visited, kstop,
-                                    False, table_slots)
+                                    False, table_slots, prepared)
     return oi, od, ctr, status
 
 

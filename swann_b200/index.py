@@ -34,6 +34,8 @@ TABLE_BUDGET = 24 << 30
 COPY_CHUNK = 8192
 # blocks of at least this many queries are searched in locality order (below)
 LOCALITY_MIN = 1024
+# ... and have their shared tables cleared on a side stream during the seed selection
+PREPARE_AHEAD_MIN = 1024
 
 
 @dataclass
@@ -204,17 +206,31 @@ class Index:
         `locality`); appends (ids, dist) in input order to `outs` and each
         launch's (counters, status) to `checks`.  `ent`: the seeds' catalogue
         indices when already selected."""
+        nq = Qd.shape[0]
+        step = max(1, min(nq, TABLE_BUDGET // (8 * Hc)))
+        prep = None
+        if nq >= PREPARE_AHEAD_MIN and step == nq:
+            # one launch: clear its shared tables on a side stream while the
+            # seeds are selected and sorted
+            comp = torch.cuda.current_stream(r.dev)
+            side = self._side_stream(r.dev, "prepare")
+            side.wait_stream(comp)
+            E.prepare_lean(nq, cfg.branches, cfg.budget, r.G.shape[1], r.dev, side, table_slots=Hc)
+            prep = torch.cuda.Event()
+            prep.record(side)
         if ent is None:
             ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
         seeds = r.catalogue[ent].to(torch.int32)
         order = self.locality_order(ent, r)
         if order is not None:
             Qd, seeds = Qd[order].contiguous(), seeds[order].contiguous()
-        step = max(1, min(Qd.shape[0], TABLE_BUDGET // (8 * Hc)))
         part = []
-        for c0 in range(0, Qd.shape[0], step):
-            c1 = min(Qd.shape[0], c0 + step)
-            ids, dist, ctr, status = _search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc)
+        for c0 in range(0, nq, step):
+            c1 = min(nq, c0 + step)
+            if prep is not None:
+                torch.cuda.current_stream(r.dev).wait_event(prep)
+            ids, dist, ctr, status = _search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc,
+                                                    prepared=prep is not None)
             part.append((ids, dist))
             checks.append((ctr, status))
         ids = torch.cat([p[0] for p in part]) if len(part) > 1 else part[0][0]
@@ -236,8 +252,11 @@ class Index:
         return torch.argsort(key, stable=True)
 
     def _copy_stream(self, dev):
-        streams = self.__dict__.setdefault("_copy_streams", {})
-        key = torch.device(dev).index
+        return self._side_stream(dev, "copy")
+
+    def _side_stream(self, dev, role):
+        streams = self.__dict__.setdefault("_side_streams", {})
+        key = (torch.device(dev).index, role)
         if key not in streams:
             streams[key] = torch.cuda.Stream(device=dev)
         return streams[key]
@@ -300,7 +319,7 @@ def _catalogue_tour(cat_rows, metric):
     return torch.from_numpy(pos)
 
 
-def _search_device(r: _Replica, Qd, seeds, k, cfg, metric, table_slots):
+def _search_device(r: _Replica, Qd, seeds, k, cfg, metric, table_slots, prepared=False):
     """The fused search on one replica: shared table, bound and claims on,
     per-branch visited tables elided (swann/index.py:105-109).
 
@@ -315,7 +334,7 @@ def _search_device(r: _Replica, Qd, seeds, k, cfg, metric, table_slots):
     return E.search_fused_lean(
         r.X, r.G, Qd, seeds, k=k, L=cfg.queue, B=cfg.budget, metric=metric, team_size=cfg.team,
         stop_eps=cfg.stop_eps, shared_cache=True, shared_bound=True, exclusive=2, elide_visited=True,
-        table_slots=table_slots)
+        table_slots=table_slots, prepared=prepared)
 
 
 def _as_cuda(a) -> torch.Tensor:
