@@ -4,14 +4,16 @@
 Workload (the north star's headline): n = 1,000,000 rows,
 d = 1536, drawn from 1,000 anisotropic Gaussian clusters (per-dimension scales
 log-uniform in [0.1, 1]), rows L2-normalised and stored fp16; fp32 queries
-normalised from the same mixture; inner product; k = 10; a batch of 65,535
-queries per GPU per step; degree-64 graph (candidates 128, alpha 1.2) built by
-this package's kernels.  Seeded synthetic data stands in for the corpora the
-reference measured on.
+normalised from the same mixture; inner product; k = 10; a global batch of
+65,535 queries per step, split across the GPUs in contiguous shards (strong
+scaling; the per-GPU-fixed weak figure is reported beside it for N > 1);
+degree-64 graph (candidates 128, alpha 1.2) built by this package's kernels.
+Seeded synthetic data stands in for the corpora the reference measured on.
 
-A step is one Index.search of the batch.  The operating point (branches,
-queue, stop_eps) is the fastest one whose recall@10 against exact fp32 ground
-truth is >= 0.95, chosen before timing on a fixed subset of the batch.
+A step is one Index.search of each GPU's shard.  The operating point
+(branches, queue, stop_eps) is the fastest one whose recall@10 against exact
+fp32 ground truth is >= 0.95, chosen before timing on a fixed subset of the
+batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
@@ -75,7 +77,11 @@ TARGET = 0.95
 # ---------------------------------------------------------------------------
 # synthetic data (seeded, generated on the device in chunks)
 
-def gen_mixture(n, d, clusters, seed, dev, half, normalise, aniso=True, chunk=1 << 16, sigma=0.3):
+def gen_mixture(n, d, clusters, seed, dev, half, normalise, aniso=True, chunk=1 << 16, sigma=0.3, rows=None):
+    """Rows [r0, r1) (default all n) of a seeded Gaussian-mixture corpus.  The
+    mixture (centres, scales) comes from one fixed seed; each 65536-row chunk
+    draws from its own stream (seed, chunk), so a rank can generate exactly its
+    own row block and get the same rows a single process would."""
     g = torch.Generator(device=dev)
     g.manual_seed(1234)   # the mixture itself is shared by corpus and queries
     if clusters:
@@ -85,34 +91,35 @@ def gen_mixture(n, d, clusters, seed, dev, half, normalise, aniso=True, chunk=1 
             scales = torch.exp(lo + (hi - lo) * torch.rand((clusters, d), generator=g, device=dev))
         else:
             scales = torch.full((clusters, d), sigma, device=dev)
+    r0, r1 = (0, n) if rows is None else rows
+    out = torch.empty((r1 - r0, d), dtype=torch.float16 if half else torch.float32, device=dev)
     gs = torch.Generator(device=dev)
-    gs.manual_seed(seed)
-    out = torch.empty((n, d), dtype=torch.float16 if half else torch.float32, device=dev)
-    for a in range(0, n, chunk):
-        b = min(n, a + chunk)
+    for c in range(r0 // chunk, (r1 + chunk - 1) // chunk):
+        a, b = c * chunk, min(n, (c + 1) * chunk)
+        gs.manual_seed(seed * 1_000_003 + c)
         z = torch.randn((b - a, d), generator=gs, device=dev)
         if clusters:
-            c = torch.randint(0, clusters, (b - a,), generator=gs, device=dev)
-            x = centres[c] + scales[c] * z
+            cl = torch.randint(0, clusters, (b - a,), generator=gs, device=dev)
+            x = centres[cl] + scales[cl] * z
         else:
             x = z
         if normalise:
             x = x / x.norm(dim=1, keepdim=True)
-        out[a:b] = x.to(out.dtype)
+        lo, hi = max(a, r0), min(b, r1)
+        out[lo - r0:hi - r0] = x[lo - a:hi - a].to(out.dtype)
     return out
 
 
-def make_corpus(cfg, dev):
+def make_corpus(cfg, dev, rows=None):
     aniso = cfg["metric"] == "ip"
     norm = cfg["metric"] == "ip"
-    X = gen_mixture(cfg["n"], cfg["d"], cfg["clusters"], 1, dev, cfg["half"], norm, aniso=aniso)
-    return X
+    return gen_mixture(cfg["n"], cfg["d"], cfg["clusters"], 1, dev, cfg["half"], norm, aniso=aniso, rows=rows)
 
 
-def make_queries(cfg, dev, rank, batch):
+def make_queries(cfg, dev, seed, batch):
     aniso = cfg["metric"] == "ip"
     norm = cfg["metric"] == "ip"
-    return gen_mixture(batch, cfg["d"], cfg["clusters"], 1000 + rank, dev, False, norm, aniso=aniso)
+    return gen_mixture(batch, cfg["d"], cfg["clusters"], seed, dev, False, norm, aniso=aniso)
 
 
 @torch.no_grad()
@@ -252,7 +259,8 @@ def max_over_ranks(x, world):
 
 def build_index(cfg, dev, world, rank):
     """The graph by this package's kernels: single GPU, or row blocks over
-    the ranks with NCCL all-gathers (swann_b200.dist.build_sharded)."""
+    the ranks with NCCL all-gathers (swann_b200.dist.build_sharded); under
+    torchrun each rank generates only its own row block of the corpus."""
     from swann_b200 import build as B
     from swann_b200 import dist as D
     t = {}
@@ -277,10 +285,8 @@ def build_index(cfg, dev, world, rank):
         torch.cuda.synchronize()
         t["reverse_s"] = time.perf_counter() - t1
     else:
-        Xfull = make_corpus(cfg, dev)   # each rank keeps only its row block as its "input"
         a, b = D.shard_bounds(n, world)[rank]
-        Xl = Xfull[a:b].contiguous()
-        del Xfull
+        Xl = make_corpus(cfg, dev, rows=(a, b))   # this rank's row block is its input
         torch.cuda.synchronize()
         t["generate_s"] = time.perf_counter() - t0
         stage = {}
@@ -313,10 +319,36 @@ def build_index(cfg, dev, world, rank):
     return X, G, t
 
 
+def sweep_roofline(build_t, n, d, half):
+    """The candidate sweep against the tensor pipe: 2 n^2 d FLOPs (counted as
+    written) over the measured sustained bf16 GEMM rate for fp16 rows
+    (kind::f16), or a sixth of it for fp32 rows (3xTF32: three tf32 MMAs per
+    product at half the bf16 rate)."""
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    sustained = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    kind = "measured" if "bf16_tflops_sustained" in peaks else "fallback"
+    div = 1.0 if half else 6.0
+    flops = 2.0 * n * n * d
+    sec = build_t.get("sweep_s")
+    if not sec:
+        return None
+    achieved = flops / sec / 1e12
+    return {"bound": "tensor", "kernel": "swb::sweep::sweep_kernel", "achieved": round(achieved, 1),
+            "peak": round(sustained / div, 1), "unit": "TFLOP/s", "frac": round(achieved / (sustained / div), 4),
+            "peak_source": f"{kind} bf16_tflops_sustained" + ("" if half else " / 6 (3xTF32)"), "flops": flops}
+
+
+def sample_rows(total, m):
+    """m row indices spread evenly over [0, total): a sample that follows the
+    batch's own order (the input order, not the locality order)."""
+    m = max(1, min(int(m), total))
+    return np.unique(np.linspace(0, total - 1, m).round().astype(np.int64))
+
+
 def cpu_baseline(X, G, Q, seeds, cfg, op, budget_s=15.0):
     """The reference's CPU search path (swann/_refcpu.py, restated in C by the
     oracle) on the host cores: independent branches, merged; timed on a
-    bounded sample of the batch."""
+    bounded sample of the batch spread evenly over it in input order."""
     from oracle import oracle as O
     Xh = X.float().cpu().numpy() if X.dtype == torch.float16 else X.cpu().numpy()
     Gh = G.cpu().numpy()
@@ -327,51 +359,122 @@ def cpu_baseline(X, G, Q, seeds, cfg, op, budget_s=15.0):
     metric = 0 if cfg["metric"] == "ip" else 1
     kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=metric, team=16, vec=vec, stop_eps=op["stop_eps"],
               kstop=min(cfg["k"], op["queue"]), threads=cores)
-    m = cores * 2
+    pick = sample_rows(Qh.shape[0], cores * 2)
     t = time.perf_counter()
-    O.search(Xh, Gh, Qh[:m], Sh[:m], **kw)
+    O.search(Xh, Gh, Qh[pick], Sh[pick], **kw)
     el = time.perf_counter() - t
-    m2 = int(min(Qh.shape[0], max(m, m * budget_s / max(el, 1e-3))))
+    pick = sample_rows(Qh.shape[0], max(len(pick), len(pick) * budget_s / max(el, 1e-3)))
     t = time.perf_counter()
-    O.search(Xh, Gh, Qh[:m2], Sh[:m2], **kw)
+    O.search(Xh, Gh, Qh[pick], Sh[pick], **kw)
     el = time.perf_counter() - t
-    return {"value": m2 / el, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"{m2} queries of the timed batch, the reference's CPU search (independent branches, "
-                      f"_refcpu semantics) at the chosen branches/queue/stop_eps, C oracle on {cores} threads",
-            "seconds": el}
+    return {"value": round(len(pick) / el, 2), "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{len(pick)} queries spread evenly over the timed batch in input order; the reference's CPU "
+                      f"search (independent branches, _refcpu semantics) at the chosen branches/queue/stop_eps, "
+                      f"C oracle on {cores} threads",
+            "seconds": round(el, 3)}
 
 
-# per-query table slots per claim of the busiest query (then a power of two);
-# the clear of the table is a full write of it every step
-TABLE_HEADROOM = 1.5
+def exact_distance_error(X, Q, ids, dist, metric):
+    """Largest relative gap between the returned distances and an exact
+    (float64) recomputation from the stored rows."""
+    ids = ids.to(torch.int64)
+    ok = ids >= 0
+    x = X[ids.clamp(min=0)].double()
+    q = Q.double()[:, None, :]
+    ex = 1.0 - (q * x).sum(-1) if metric == "ip" else ((q - x) ** 2).sum(-1)
+    rel = (dist.double() - ex).abs() / ex.abs().clamp(min=1e-30)
+    return float(rel[ok].max()) if bool(ok.any()) else 0.0
 
 
-def table_slots_for(claims):
-    from swann_b200 import _engine as E
-    return max(4096, E.next_pow2(int(TABLE_HEADROOM * claims)))
+def reference_package():
+    """The reference package installed under baseline/_ref (baseline/install.sh),
+    or None."""
+    path = ROOT / "baseline" / "_ref"
+    if not (path / "swann" / "__init__.py").exists():
+        return None
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    import swann
+    return swann
 
 
-def calibrate(index, Qs, truth, cfg):
-    """Fastest (branches, queue, stop_eps) with recall >= TARGET on Qs."""
+def reference_kernels_for(swann_ref):
+    """Hands the reference's engine its own kernels.  The reference compiles
+    swann/csrc/local_search.cu on first use (swann/_engine.py:42-63) for the
+    architecture TORCH_CUDA_ARCH_LIST names, 12.0 unless set; here the same
+    source, compiled with the same flags for sm_100a (oracle/_ref), fills the
+    engine's extension slot, so its Python path runs unmodified.  Without that
+    build the reference compiles itself for this GPU.  Returns a description."""
+    from oracle import oracle as O
+    K = O.ref_kernels()
+    if K is not None:
+        swann_ref._engine._EXT = K
+        return "swann/csrc/local_search.cu compiled unmodified for sm_100a (oracle/_ref)"
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    swann_ref._engine.ext()
+    return "swann/csrc/local_search.cu compiled by the reference's own ext() for sm_100a"
+
+
+def time_reference_gpu(ref_index, Qd, k, op, reps=3):
+    """The reference's Index.search (its seed selection, engine, kernels and
+    the copy of the answers to the host) on a device-resident batch; wall
+    clock around synchronous calls (it returns numpy arrays)."""
+    kw = dict(k=k, branches=op["branches"], queue=op["queue"], stop_eps=op["stop_eps"])
+    ref_index.search(Qd, **kw)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        ref_index.search(Qd, **kw)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t)
+    return statistics.median(ts)
+
+
+def reference_gpu_leg(X, G, catalogue, Qall, truth, gt_n, cfg, op):
+    """The same-box GPU bar: the reference's own Index.search on this graph,
+    catalogue and operating point -- recall@10 on the ground-truth sample and
+    QPS on the whole batch."""
+    swann_ref = reference_package()
+    if swann_ref is None:
+        return {"unavailable": "the reference package is not installed under baseline/_ref (baseline/install.sh)"}
+    impl = reference_kernels_for(swann_ref)
+    ref_index = swann_ref.Index(X, G, metric=cfg["metric"], catalogue=catalogue)
+    ids, _ = ref_index.search(Qall[:gt_n], k=cfg["k"], branches=op["branches"], queue=op["queue"],
+                              stop_eps=op["stop_eps"])
+    rec = recall(ids[:, :10], truth[:, :10], 10)
+    sec = time_reference_gpu(ref_index, Qall, cfg["k"], op)
+    del ref_index
+    torch.cuda.empty_cache()
+    return {"qps": round(Qall.shape[0] / sec, 1), "ms_per_batch": round(sec * 1e3, 3), "batch": int(Qall.shape[0]),
+            "recall@10": round(rec, 4), "impl": "swann/index.py Index.search (exclusive claims, the reference's "
+                                                "table sizing) over " + impl,
+            "timing": "wall clock around the synchronous call (device-resident queries, answers to the host), "
+                      "median of 3 after one warm-up"}
+
+
+def calibrate(search, Qs, truth, cfg):
+    """Fastest (branches, queue, stop_eps) with recall >= TARGET on Qs;
+    search(Qs, k, branches, queue, stop_eps) -> ids (host or device)."""
     best = None
     tried = []
     for branches, queue in cfg.get("ladder", LADDER):
         found = False
         for eps in EPS:
-            ids, _ = index.search_tensors(Qs, k=cfg["k"], branches=branches, queue=queue, stop_eps=eps)
+            ids = search(Qs, cfg["k"], branches, queue, eps)
             torch.cuda.synchronize()
-            r = recall(ids.cpu().numpy()[:, :10], truth[:, :10], 10)   # the target is recall@10
+            ids = ids.cpu().numpy() if isinstance(ids, torch.Tensor) else np.asarray(ids)
+            r = recall(ids[:, :10], truth[:, :10], 10)   # the target is recall@10
             if r < TARGET:
                 tried.append((branches, queue, eps, r, None))
                 continue
             ts = []
             for _ in range(2):
-                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s0.record()
-                index.search_tensors(Qs, k=cfg["k"], branches=branches, queue=queue, stop_eps=eps)
-                s1.record()
                 torch.cuda.synchronize()
-                ts.append(s0.elapsed_time(s1))
+                t = time.perf_counter()
+                search(Qs, cfg["k"], branches, queue, eps)
+                torch.cuda.synchronize()
+                ts.append((time.perf_counter() - t) * 1e3)
             tried.append((branches, queue, eps, r, min(ts)))
             if best is None or min(ts) < best[4]:
                 best = (branches, queue, eps, r, min(ts))
@@ -380,6 +483,54 @@ def calibrate(index, Qs, truth, cfg):
         if found and best is not None and branches >= 64:
             break
     return best, tried
+
+
+def choose_op(args, search, Qs, truth, cfg, rank, world):
+    """The operating point: --fixed, or calibrated on rank 0 and shared."""
+    if args.fixed:
+        b, q, e = args.fixed.split(",")
+        return dict(branches=int(b), queue=int(q), stop_eps=float(e)), []
+    op, tried = None, []
+    if rank == 0:
+        best, tried = calibrate(search, Qs, truth, cfg)
+        if best is None:
+            best = max(tried, key=lambda t: t[3])
+        op = dict(branches=best[0], queue=best[1], stop_eps=best[2])
+    if world > 1:
+        import torch.distributed as dist
+        box = [op]
+        dist.broadcast_object_list(box, src=0)
+        op = box[0]
+    return op, tried
+
+
+def timed_steps(step, steps, warmup, world, local, sample_clocks=True):
+    """W untimed steps, then K steps bracketed by a barrier and a device
+    synchronisation on both sides, timed with CUDA events on the launching
+    stream; the max over ranks."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local) if sample_clocks else None
+    if clk:
+        clk.__enter__()
+    try:
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    finally:
+        if clk:
+            clk.__exit__(None, None, None)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    return ms, (clk.summary() if clk else None)
 
 
 def run(args):
@@ -391,77 +542,49 @@ def run(args):
     import swann_b200 as swann
     from swann_b200 import _engine as E
     from swann_b200 import _select as S
+    from swann_b200 import dist as D
 
     X, G, build_t = build_index(cfg, dev, world, rank)
     torch.cuda.empty_cache()
     index = swann.Index(X, G, metric=cfg["metric"], catalogue_size=cfg.get("catalogue", 4096))
-    batch = cfg["batch"]
-    Q = make_queries(cfg, dev, rank, batch)
+    batch = cfg["batch"]                                   # the global batch of one step
+    Qall = make_queries(cfg, dev, 1000, batch)             # the same on every rank
+    a, b = D.shard_bounds(batch, world)[rank]
+    Q = Qall[a:b].contiguous()                             # this rank's shard
     gt_n = min(batch, args.gt)
-    truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
+    truth = exact_topk(X, Qall[:gt_n], cfg["k"], cfg["metric"]) if rank == 0 else None
 
-    # operating point: chosen on rank 0, shared (or fixed on the command line)
-    if args.fixed:
-        b, q, e = args.fixed.split(",")
-        op, tried = dict(branches=int(b), queue=int(q), stop_eps=float(e)), []
-    elif rank == 0:
-        best, tried = calibrate(index, Q[:gt_n], truth, cfg)
-        if best is None:
-            best = max(tried, key=lambda t: t[3])
-        op = dict(branches=best[0], queue=best[1], stop_eps=best[2])
-    else:
-        op, tried = None, []
-    if world > 1 and not args.fixed:
-        import torch.distributed as dist
-        box = [op]
-        dist.broadcast_object_list(box, src=0)
-        op = box[0]
+    def my_search(Qs, k, branches, queue, eps):
+        return index.search_tensors(Qs, k=k, branches=branches, queue=queue, stop_eps=eps)[0]
 
-    # Size the per-query distance table from what the queries actually claim:
-    # TABLE_HEADROOM times the busiest query's claims, a power of two (load
-    # <= 67% for that query, ~15% for a typical one).  A probe run that finds
-    # no slot scores the row uncached, so a fuller table costs dedup, not results.
-    ent = S.select_nearest(Q[:gt_n], index._cat, op["branches"], metric=index._m)
-    sd = index.catalogue[ent].to(torch.int32)
-    _, _, ctr, _ = E.search_fused_lean(X, G, Q[:gt_n], sd, k=cfg["k"], L=op["queue"], B=64, metric=index._m,
-                                       team_size=16, stop_eps=op["stop_eps"], shared_cache=True,
-                                       shared_bound=True, exclusive=2, elide_visited=True)
-    claims = (ctr[..., 5].to(torch.int64).sum(1) + op["branches"]).max().item()
-    ref_slots = E.cache_size(op["branches"], 64, G.shape[1])
-    slots = min(ref_slots, table_slots_for(claims))
-    index.table_slots = slots
-    table = {"slots": slots, "reference_slots": ref_slots, "max_claims_per_query": int(claims),
-             "max_load": round(claims / slots, 4)}
+    op, tried = choose_op(args, my_search, Qall[:gt_n], truth, cfg, rank, world)
+
+    # recall and exact distances at the operating point, on the ground-truth sample
+    checks = {}
+    if rank == 0:
+        ids_s, dist_s = index.search_tensors(Qall[:gt_n], k=cfg["k"], **op)
+        got = ids_s.cpu().numpy()
+        checks["recall@10"] = round(recall(got[:, :10], truth[:, :10], 10), 4)
+        if cfg["k"] != 10:
+            checks[f"recall@{cfg['k']}"] = round(recall(got, truth, cfg["k"]), 4)
+        checks["max_rel_dist_err"] = exact_distance_error(X, Qall[:gt_n], ids_s, dist_s, cfg["metric"])
 
     def step():
         return index.search_tensors(Q, k=cfg["k"], **op)
 
-    # recall of the full-batch operating point, on the ground-truth subset
-    ids, _ = step()
-    torch.cuda.synchronize()
-    got = ids[:gt_n].cpu().numpy()
-    rec = recall(got[:, :10], truth[:, :10], 10)
-    rec_k = recall(got, truth, cfg["k"])
+    # -- device-resident timing (value): strong scaling, the global batch split
+    ms, clocks = timed_steps(step, args.steps, args.warmup, world, local)
+    value = batch * args.steps / (ms / 1e3)
 
-    # -- device-resident timing (value) ----------------------------------
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
-        barrier(world)
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    clocks = clk.summary()
-    value = world * batch * args.steps / (ms / 1e3)
+    # -- weak scaling beside it (N > 1): a full batch on every GPU ----------
+    weak = None
+    if world > 1:
+        Qw = make_queries(cfg, dev, 2000 + rank, batch)
+        ms_w, _ = timed_steps(lambda: index.search_tensors(Qw, k=cfg["k"], **op), args.steps, args.warmup, world,
+                              local, sample_clocks=False)
+        weak = {"value": round(world * batch * args.steps / (ms_w / 1e3), 1), "unit": "queries/s",
+                "batch_per_gpu": batch, "ms_per_step": round(ms_w / args.steps, 3)}
+        del Qw
 
     # -- end to end through the public API with host buffers -------------
     Qh = Q.cpu().pin_memory()
@@ -474,50 +597,51 @@ def run(args):
         out_ids, out_d = index.search(Qh, k=cfg["k"], **op)
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e = {"value": world * batch * args.steps / e2e_s, "unit": "queries/s",
+    e2e = {"value": round(batch * args.steps / e2e_s, 1), "unit": "queries/s",
            "h2d_bytes_per_step": int(Qh.numel() * Qh.element_size()),
-           "d2h_bytes_per_step": int(out_ids.nbytes + out_d.nbytes)}
+           "d2h_bytes_per_step": int(out_ids.nbytes + out_d.nbytes),
+           "timing": "wall clock, host pinned queries to numpy answers, max over ranks"}
 
-    # -- roofline of the dominant kernel (the fused search) ----------------
+    # -- roofline of the dominant kernel (the fused search) on this rank's shard
+    nq = Q.shape[0]
     ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
     seeds = index.catalogue[ent].to(torch.int32)
-    order = index.locality_order(ent)   # the order Index.search runs the batch in
-    if order is not None:
-        Q, seeds = Q[order].contiguous(), seeds[order].contiguous()
+    order = index.locality_order(ent)   # the order Index.search runs the block in
+    Qo, so = (Q[order].contiguous(), seeds[order].contiguous()) if order is not None else (Q, seeds)
+    slots = index.table_slots_for(op["branches"], 64, op["queue"], op["stop_eps"], G.shape[1])
     kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=index._m, team_size=16, stop_eps=op["stop_eps"],
               shared_cache=True, shared_bound=True, exclusive=2, elide_visited=True, table_slots=slots)
-    _, _, ctr, _ = E.search_fused_lean(X, G, Q, seeds, **kw)
+    _, _, ctr, _ = E.search_fused_lean(X, G, Qo, so, **kw)
     torch.cuda.synchronize()
     c = ctr.to(torch.int64)
-    nodes = int(c[..., 5].sum()) + int(batch * op["branches"])      # claimed + seeds
+    nodes = int(c[..., 5].sum()) + int(nq * op["branches"])      # claimed + seeds
     exps = int(c[..., 0].sum())
+    claims = int((c[..., 5].sum(1) + op["branches"]).max())
     esize = X.element_size()
     alg_bytes = nodes * cfg["d"] * esize + exps * G.shape[1] * 4
     lib = E.N.lib()
+    stream = torch.cuda.current_stream()
+    Jq, kk = op["branches"], min(cfg["k"], op["queue"])
+    cache = E._WS.get("cache", nq * slots, torch.int64, dev).view(nq, -1)
+    bound = E._WS.get("bound", nq, torch.float32, dev)
+    qdone = E._WS.get("qdone", nq, torch.int32, dev)
+    bi = E._WS.get("branch_ids", nq * Jq * kk, torch.int32, dev)
+    bd = E._WS.get("branch_dist", nq * Jq * kk, torch.float32, dev)
+    oi = torch.empty((nq, cfg["k"]), dtype=torch.int32, device=dev)
+    od = torch.empty((nq, cfg["k"]), dtype=torch.float32, device=dev)
     kt = []
     for _ in range(max(3, args.steps)):
         # prepare + fused, each bracketed by events on the launching stream
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        Jq = op["branches"]
-        Hc = slots
-        cache = E._WS.get("cache", batch * Hc, torch.int64, dev).view(batch, -1)
-        bound = E._WS.get("bound", batch, torch.float32, dev)
-        qdone = E._WS.get("qdone", batch, torch.int32, dev)
-        kk = min(cfg["k"], op["queue"])
-        bi = E._WS.get("branch_ids", batch * Jq * kk, torch.int32, dev)
-        bd = E._WS.get("branch_dist", batch * Jq * kk, torch.float32, dev)
-        oi = torch.empty((batch, cfg["k"]), dtype=torch.int32, device=dev)
-        od = torch.empty((batch, cfg["k"]), dtype=torch.float32, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
         s = stream.cuda_stream
         ev[0].record(stream)
-        E.N.check(lib.swb_search_prepare(batch, E.N.ptr(cache), Hc, E.N.ptr(bound), E.N.ptr(qdone), s))
+        E.N.check(lib.swb_search_prepare(nq, E.N.ptr(cache), slots, E.N.ptr(bound), E.N.ptr(qdone), s))
         ev[1].record(stream)
         rc = lib.swb_search_fused(
-            E.N.ptr(X), E.N.dtype_code(X), X.shape[0], X.shape[1], E.N.ptr(G), G.shape[1], E.N.ptr(Q),
-            E.N.ptr(seeds), batch, Jq, 1, cfg["k"], op["queue"], 64, index._m, 16, 0, float(op["stop_eps"]),
-            cfg["k"], None, 1, E.N.ptr(cache), Hc, E.N.ptr(bound), 2, 0, 0.0, E.N.ptr(bi), E.N.ptr(bd),
-            E.N.ptr(qdone), E.N.ptr(oi), E.N.ptr(od), None, None, None, None, None, E.N.ptr(status), s)
+            E.N.ptr(X), E.N.dtype_code(X), X.shape[0], X.shape[1], E.N.ptr(G), G.shape[1], E.N.ptr(Qo),
+            E.N.ptr(so), nq, Jq, 1, cfg["k"], op["queue"], 64, index._m, 16, 0, float(op["stop_eps"]),
+            cfg["k"], None, 1, E.N.ptr(cache), slots, E.N.ptr(bound), 2, 0, 0.0, E.N.ptr(bi), E.N.ptr(bd),
+            E.N.ptr(qdone), E.N.ptr(oi), E.N.ptr(od), None, None, None, None, None, None, s)
         E.N.check(rc)
         ev[2].record(stream)
         torch.cuda.synchronize()
@@ -529,13 +653,13 @@ def run(args):
     prof = profile_traffic(f"search_fused_{args.config}")
     traffic, traffic_src = None, None
     if prof:
-        same = prof.get("batch") == batch and prof.get("op") == [op["branches"], op["queue"], op["stop_eps"]]
+        same = prof.get("batch") == nq and prof.get("op") == [op["branches"], op["queue"], op["stop_eps"]]
         if same:
             traffic, traffic_src = prof["traffic_per_launch"], "ncu, this launch shape: " + prof["source"]
         else:   # same kernel and corpus, another batch or operating point: scale by this run's bytes
             traffic = round(prof["traffic_over_algorithmic"] * alg_bytes)
-            traffic_src = "ncu traffic/algorithmic ratio %.3f x this run's algorithmic bytes (%s)" % (
-                prof["traffic_over_algorithmic"], prof["source"])
+            traffic_src = "ncu traffic/algorithmic ratio %.3f (batch %s) x this run's algorithmic bytes (%s)" % (
+                prof["traffic_over_algorithmic"], prof.get("batch"), prof["source"])
     roofline = {"bound": "hbm", "kernel": "swb::fused_kernel", "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                 "traffic": traffic, "traffic_source": traffic_src,
@@ -544,32 +668,53 @@ def run(args):
                 "dram_gbs": round(traffic / (fused_ms / 1e3) / 1e9, 1) if traffic else None,
                 "dram_frac": round(traffic / (fused_ms / 1e3) / 1e9 / peak, 4) if traffic else None,
                 "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": round(fused_ms, 3),
-                "prepare_ms": round(prep_ms, 3),
-                "per_query": {"distinct_nodes_scored": nodes / batch, "expansions": exps / batch}}
+                "prepare_ms": round(prep_ms, 3), "launch_batch": nq,
+                "per_query": {"distinct_nodes_scored": nodes / nq, "expansions": exps / nq}}
+    table = {"slots": slots, "reference_slots": E.cache_size(op["branches"], 64, G.shape[1]),
+             "max_claims_per_query": claims, "max_load": round(claims / slots, 4),
+             "sizing": "Index default: measured claims x 1.5, a power of two (first call: the reference's size)"}
 
     line = {
-        "metric": f"QPS at recall@10>={TARGET} ({cfg['desc']}, batch {batch} per GPU)",
+        "metric": f"QPS at recall@10>={TARGET} ({cfg['desc']}, global batch {batch})",
         "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
         "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], "storage": "f16" if cfg["half"] else "f32",
-                   "metric": cfg["metric"], "batch_per_gpu": batch, "k": cfg["k"], **op, "budget": 64, "team": 16,
-                   "recall@10": round(rec, 4), **({f"recall@{cfg['k']}": round(rec_k, 4)} if cfg["k"] != 10 else {}),
-                   "recall_sample": gt_n, "graph": "degree 64, candidates 128, alpha 1.2",
-                   "catalogue": int(index.catalogue.numel()),
-                   "claims": "strict (exclusive=2)", "table": table,
+                   "metric": cfg["metric"], "global_batch": batch, "batch_per_gpu": b - a, "k": cfg["k"], **op,
+                   "budget": 64, "team": 16, **checks, "recall_sample": gt_n,
+                   "graph": "degree 64, candidates 128, alpha 1.2",
+                   "catalogue": int(index.catalogue.numel()), "claims": "strict (exclusive=2)", "table": table,
                    "query_order": "nearest catalogue entry" if index.locality else "input",
                    "l2": "inputs larger than L2 (corpus %.1f GB; rows gathered at random)" % (
                        X.numel() * X.element_size() / 1e9),
                    "parallelism": f"query shards x{world}, replicas"},
-        "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": 2 * args.steps,
-        "build": {k: round(v, 3) for k, v in build_t.items()},
-        "calibration": [{"branches": b, "queue": q, "stop_eps": e, "recall": round(r, 4),
-                         "ms": None if t is None else round(t, 3)} for b, q, e, r, t in tried],
+        "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": 3 * args.steps,
+        "gpu_launches_per_step": "sel::topk_kernel (seed top-E), swb::prepare_kernel (table clear), "
+                                 "swb::fused_kernel (search); plus library GEMM/sort/gather launches",
+        "build": {**{k: round(v, 3) for k, v in build_t.items()},
+                  "roofline": sweep_roofline(build_t, cfg["n"], cfg["d"], cfg["half"]) if world == 1 else None},
+        "calibration": [{"branches": b_, "queue": q, "stop_eps": e, "recall": round(r, 4),
+                         "ms": None if t is None else round(t, 3)} for b_, q, e, r, t in tried],
     }
+    if weak:
+        line["weak"] = weak
     if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(X, G, Q, seeds, cfg, op)
+        # a sample spread over the batch in input order, with the seeds Index.search selects
+        pick = torch.from_numpy(sample_rows(batch, 4096)).to(dev)
+        Qs = Qall[pick].contiguous()
+        sd = index.catalogue[S.select_nearest(Qs, index._cat, op["branches"], metric=index._m)].to(torch.int32)
+        line["cpu_baseline"] = cpu_baseline(X, G, Qs, sd, cfg, op)
+    if rank == 0 and world == 1 and not args.no_ref:
+        del cache, bound, qdone, bi, bd
+        E._WS.bufs.clear()
+        torch.cuda.empty_cache()
+        refk = reference_gpu_leg(X, G, index.catalogue, Qall, truth, gt_n, cfg, op)
+        line["reference_kernel"] = refk
+        if "qps" in refk:
+            line["vs_reference_kernel"] = {"value_ratio": round(value / refk["qps"], 3),
+                                           "e2e_ratio": round(e2e["value"] / refk["qps"], 3),
+                                           "recall_delta": round(checks["recall@10"] - refk["recall@10"], 4)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -577,17 +722,91 @@ def run(args):
         dist.destroy_process_group()
 
 
+def tensor_peaks(seconds=3.0, n=8192):
+    """Measured dense fp32 GEMM rates (the build's 3xTF32 sweep has no entry
+    in MEASURED_PEAKS.json): torch.matmul fp32 with TF32 allowed, and without,
+    best of 5 (burst) and back to back for `seconds` (sustained)."""
+    a = torch.randn((n, n), device="cuda")
+    b = torch.randn((n, n), device="cuda")
+    out = {}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        for name, tf32 in (("tf32", True), ("fp32", False)):
+            torch.backends.cuda.matmul.allow_tf32 = tf32
+            for _ in range(2):
+                a @ b
+            torch.cuda.synchronize()
+            best = 1e9
+            for _ in range(5):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                a @ b
+                e1.record()
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            flops = 2.0 * n ** 3
+            reps = max(1, int(seconds * 1e3 / best))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                a @ b
+            e1.record()
+            torch.cuda.synchronize()
+            out[f"{name}_tflops"] = round(flops / (best / 1e3) / 1e12, 1)
+            out[f"{name}_tflops_sustained"] = round(flops * reps / (e0.elapsed_time(e1) / 1e3) / 1e12, 1)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    torch.cuda.empty_cache()
+    return out
+
+
+def candidate_parity(X, cand, cdist, metric, rows=48, rel=1e-6):
+    """Build parity at full size: for a sample of rows spread over the corpus,
+    the exact candidate lists (every column, in float64, the oracle's
+    knn_candidates) against the sweep's.  A position may differ only where the
+    two lists' distances there are exact ties within `rel` relative distance.
+    Returns the count of other differences (the gate: 0) and the largest
+    relative gap between the sweep's fp32 distance and the exact one."""
+    from oracle import oracle as O
+    n, C = cand.shape
+    pick = sample_rows(n, rows)
+    Xh = X.float().cpu().numpy()
+    m = 0 if metric == "ip" else 1
+    mism, worst, ties = 0, 0.0, 0
+    t0 = time.perf_counter()
+    for r in pick:
+        idx, dst, d64 = O.knn_candidates(Xh, C, m, rows=(int(r), int(r) + 1), threads=O.cpu_count(), exact64=True)
+        mine = cand[int(r)].cpu().numpy()
+        mine_d = cdist[int(r)].cpu().numpy().astype(np.float64)
+        want = idx[0]
+        # exact distances of the sweep's own picks
+        xr = Xh[int(r)].astype(np.float64)
+        xs = Xh[mine].astype(np.float64)
+        ex = 1.0 - xs @ xr if m == 0 else np.maximum(((xs - xr) ** 2).sum(1), 0.0)
+        scale = np.maximum(np.abs(d64[0]), 1e-30)
+        worst = max(worst, float(np.max(np.abs(mine_d - ex) / np.maximum(np.abs(ex), 1e-30))))
+        for p in np.nonzero(mine != want)[0]:
+            if abs(ex[p] - d64[0][p]) <= rel * scale[p]:
+                ties += 1
+            else:
+                mism += 1
+    return {"rows_checked": int(len(pick)), "non_tie_mismatches": int(mism), "tie_swaps": int(ties),
+            "tie_rule": f"exact distances within {rel:g} relative", "max_rel_dist_gap": worst,
+            "oracle": "exact sweep in float64 over all columns (oracle knn_candidates)",
+            "seconds": round(time.perf_counter() - t0, 1)}
+
+
 def run_build(args):
-    """Graph build seconds (sweep / prune / reverse) on one GPU, with the sweep
-    against the tensor pipe: 2 n^2 d FLOPs over the measured dense bf16 peak
-    for fp16 rows (kind::f16), a sixth of it for fp32 rows (3xTF32 issues three
-    tf32 MMAs per product at half the bf16 rate).  The sweep runs for seconds
-    under the 1 kW power cap, so the denominator is the sustained GEMM figure;
-    the fraction of the burst figure is reported beside it."""
+    """Graph build seconds (sweep / prune / reverse) on one GPU, the sweep
+    against the tensor pipe (measured sustained bf16 for fp16 rows; for fp32
+    rows both a sixth of it and a third of the measured sustained TF32 GEMM
+    rate), and the candidate lists of a row sample against the exact ones."""
     world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
     cfg = dict(CONFIGS[args.config])
     from swann_b200 import build as B
+    peaks_fp32 = tensor_peaks() if not cfg["half"] else None
     X = make_corpus(cfg, dev)
     torch.cuda.synchronize()
     n, d = X.shape
@@ -602,35 +821,35 @@ def run_build(args):
     G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"])
     torch.cuda.synchronize()
     t3 = time.perf_counter()
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    burst = float(peaks.get("bf16_tflops", 1590.0))
-    sustained = float(peaks.get("bf16_tflops_sustained", 1400.0))
-    flops = 2.0 * n * n * d
-    div = 1.0 if cfg["half"] else 6.0
-    ceiling = sustained / div
-    achieved = flops / (t1 - t0) / 1e12
+    roof = sweep_roofline({"sweep_s": t1 - t0}, n, d, cfg["half"])
+    if peaks_fp32:
+        roof["measured_fp32_gemm"] = peaks_fp32
+        roof["frac_of_tf32_sustained_over_3"] = round(roof["achieved"] / (peaks_fp32["tf32_tflops_sustained"] / 3), 4)
+    prune_flops = 2.0 * n * 128 * 128 * d
     line = {"metric": f"graph build seconds ({cfg['desc']}, degree 64, candidates 128, alpha 1.2)",
             "value": round(t3 - t0, 3), "unit": "s", "n_gpus": world, "higher_is_better": False,
             "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
             "config": {"workload": args.config, "n": n, "d": d, "storage": "f16" if cfg["half"] else "f32",
                        "metric": cfg["metric"], "sweep": os.environ.get("SWB_SWEEP", "mma")},
             "stages_s": {"sweep": round(t1 - t0, 3), "prune": round(t2 - t1, 3), "reverse": round(t3 - t2, 3)},
-            "roofline": {"bound": "tensor", "kernel": "swb::sweep::sweep_kernel", "achieved": round(achieved, 1),
-                         "peak": round(ceiling, 1), "unit": "TFLOP/s", "frac": round(achieved / ceiling, 4),
-                         "peak_source": ("measured bf16_tflops_sustained" if cfg["half"] else
-                                         "measured bf16_tflops_sustained / 6 (3xTF32)"),
-                         "frac_of_burst": round(achieved / (burst / div), 4), "flops": flops},
+            "roofline": roof,
+            "prune_tflops": round(prune_flops / (t2 - t1) / 1e12, 1),
             "clocks_during_sweep": clk.summary(),
             "mean_out_degree": round(float((G >= 0).sum(1).float().mean()), 2)}
+    if not args.no_cpu:
+        line["candidate_parity"] = candidate_parity(X, cand, cd, cfg["metric"])
     if rank == 0:
         print(json.dumps(line), flush=True)
 
 
 def run_reference(args):
-    """The reference's own CPU search path (the C restatement of
-    swann/_refcpu.py, independent branches merged) on the host cores, on the
-    same workload; the index is built on the GPU by this package first
-    (setup, untimed: the reference's CPU build would take days at this size)."""
+    """The reference arm: the reference package, unmodified, from baseline/_ref.
+    Its own build (swann/build.py build_graph, torch on the GPU) makes the
+    graph, its own Index selects the seeds and -- on its own kernels --
+    chooses the operating point (the fastest reaching recall@10 >= 0.95), and
+    the timed number is its CPU search path (swann/_refcpu.py, restated in C
+    by the oracle) on the host cores, on samples spread over the batch in
+    input order.  This package's library is never loaded here."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -641,54 +860,72 @@ def run_reference(args):
     cfg = dict(CONFIGS[args.config])
     if args.batch:
         cfg["batch"] = args.batch
-    import swann_b200 as swann
+    swann_ref = reference_package()
+    if swann_ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference package is not installed under "
+                                                              "baseline/_ref (baseline/install.sh)"}), flush=True)
+        return
+    from swann import _select as RS
+    from swann import build as RB
     from oracle import oracle as O
-    X, G, _ = build_index(cfg, dev, 1, 0)
-    index = swann.Index(X, G, metric=cfg["metric"], catalogue_size=cfg.get("catalogue", 4096))
-    Q = make_queries(cfg, dev, 0, cfg["batch"])
-    # the operating point of the other arm: --fixed, or the same calibration
-    # (recall >= TARGET on the ground-truth subset; untimed setup, like the build)
-    if args.fixed:
-        b, q, e = args.fixed.split(",")
-        op = dict(branches=int(b), queue=int(q), stop_eps=float(e))
-    else:
-        gt_n = min(cfg["batch"], args.gt)
-        truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
-        best, tried = calibrate(index, Q[:gt_n], truth, cfg)
-        if best is None:
-            best = max(tried, key=lambda t: t[3])
-        op = dict(branches=best[0], queue=best[1], stop_eps=best[2])
-    from swann_b200 import _select as S
-    ent = S.select_nearest(Q, index._cat, op["branches"], metric=index._m)
+    impl = reference_kernels_for(swann_ref)
+    X = make_corpus(cfg, dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    G = RB.build_graph(X, metric=cfg["metric"], degree=64, candidates=128, alpha=1.2)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    index = swann_ref.Index(X, G, metric=cfg["metric"], catalogue_size=cfg.get("catalogue", 4096))
+    Qall = make_queries(cfg, dev, 1000, cfg["batch"])
+    gt_n = min(cfg["batch"], args.gt)
+    truth = exact_topk(X, Qall[:gt_n], cfg["k"], cfg["metric"])
+
+    def ref_search(Qs, k, branches, queue, eps):
+        return index.search(Qs, k=k, branches=branches, queue=queue, stop_eps=eps)[0]
+
+    op, tried = choose_op(args, ref_search, Qall[:gt_n], truth, cfg, 0, 1)
+    ids, _ = index.search(Qall[:gt_n], k=cfg["k"], **op)
+    rec = recall(ids[:, :10], truth[:, :10], 10)
+    gpu_s = time_reference_gpu(index, Qall, cfg["k"], op)
+    ent = RS.select_nearest(Qall, index._cat, op["branches"], metric=index._m)
     seeds = index.catalogue[ent].to(torch.int32)
     Xh = X.float().cpu().numpy()
-    Gh, Qh, Sh = G.cpu().numpy(), Q.cpu().numpy(), seeds.cpu().numpy()
+    Gh, Qh, Sh = G.cpu().numpy(), Qall.cpu().numpy(), seeds.cpu().numpy()
     cores = O.cpu_count()
     metric = 0 if cfg["metric"] == "ip" else 1
     kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=metric, team=16, vec=8 if cfg["half"] else 4,
               stop_eps=op["stop_eps"], kstop=min(cfg["k"], op["queue"]), threads=cores)
     per = cores * 2
+    steps = args.warmup + args.steps
+    order = sample_rows(Qh.shape[0], per * steps)          # spread over the batch, input order
     times = []
-    for i in range(args.warmup + args.steps):
-        a = (i * per) % max(1, Qh.shape[0] - per)
+    for i in range(steps):
+        pick = order[i::steps][:per]
         t = time.perf_counter()
-        O.search(Xh, Gh, Qh[a:a + per], Sh[a:a + per], **kw)
+        O.search(Xh, Gh, Qh[pick], Sh[pick], **kw)
         if i >= args.warmup:
-            times.append(time.perf_counter() - t)
-    el = sum(times)
-    value = per * args.steps / el
-    line = {"metric": f"QPS at recall@10>={TARGET} ({cfg['desc']}, batch {cfg['batch']} per GPU)",
+            times.append((time.perf_counter() - t, len(pick)))
+    el = sum(t for t, _ in times)
+    value = sum(m for _, m in times) / el
+    line = {"metric": f"QPS at recall@10>={TARGET} ({cfg['desc']}, global batch {cfg['batch']})",
             "value": round(value, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
             "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
-            "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], **op, "budget": 64, "team": 16},
+            "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], **op, "budget": 64, "team": 16,
+                       "recall@10": round(rec, 4), "recall_sample": gt_n},
             "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": cores, "kind": "port",
-                             "sample": f"{per} queries per step (C restatement of swann/_refcpu.py, independent "
-                                       f"branches, {cores} threads); index built and the operating point "
-                                       f"calibrated on the GPU beforehand, untimed"},
+                             "sample": f"{per} queries per step spread over the batch in input order (C restatement "
+                                       f"of swann/_refcpu.py, independent branches, {cores} threads); graph by the "
+                                       f"reference's build_graph, seeds by its select_nearest, operating point "
+                                       f"calibrated on its own GPU kernels beforehand, untimed"},
             "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "reference_gpu": {"qps": round(Qall.shape[0] / gpu_s, 1), "ms_per_batch": round(gpu_s * 1e3, 3),
+                              "impl": "swann/index.py Index.search over " + impl},
+            "build_s": round(build_s, 3),
+            "calibration": [{"branches": b_, "queue": q, "stop_eps": e, "recall": round(r, 4),
+                             "ms": None if t is None else round(t, 3)} for b_, q, e, r, t in tried]}
     print(json.dumps(line), flush=True)
 
 
@@ -711,32 +948,23 @@ def run_batch_sweep(args):
     torch.cuda.empty_cache()
     index = swann.Index(X, G, metric=cfg["metric"], catalogue_size=cfg.get("catalogue", 4096))
     nmax = max(b for b, _ in BATCH_SWEEP)
-    Q = make_queries(cfg, dev, 0, nmax)
+    Q = make_queries(cfg, dev, 1000, nmax)
     gt_n = min(nmax, args.gt)
     truth = exact_topk(X, Q[:gt_n], cfg["k"], cfg["metric"])
-    from swann_b200 import _engine as E
-    from swann_b200 import _select as S
     ops = {}
     for _, br in BATCH_SWEEP:
         if br in ops:
             continue
-        index.table_slots = None
         for eps in EPS:
             ids, _ = index.search_tensors(Q[:gt_n], k=cfg["k"], branches=br, queue=12, stop_eps=eps)
             r = recall(ids.cpu().numpy()[:, :10], truth[:, :10], 10)
             if r >= TARGET:
                 break
-        # table sized from measured claims, as the main line does
-        sd = index.catalogue[S.select_nearest(Q[:gt_n], index._cat, br, metric=index._m)].to(torch.int32)
-        _, _, ctr, _ = E.search_fused_lean(X, G, Q[:gt_n], sd, k=cfg["k"], L=12, B=64, metric=index._m,
-                                           team_size=16, stop_eps=eps, shared_cache=True, shared_bound=True,
-                                           exclusive=2, elide_visited=True)
-        claims = (ctr[..., 5].to(torch.int64).sum(1) + br).max().item()
-        ops[br] = (eps, r, min(E.cache_size(br, 64, G.shape[1]), table_slots_for(claims)))
+        ops[br] = (eps, r)   # the index now sizes this configuration's table from the claims it measured
     rows = []
     for b, br in BATCH_SWEEP:
-        eps, r, slots = ops[br]
-        index.table_slots = slots
+        eps, r = ops[br]
+        slots = index.table_slots_for(br, 64, 12, eps, G.shape[1])
         kw = dict(k=cfg["k"], branches=br, queue=12, stop_eps=eps)
         reps = max(args.steps, min(200, nmax // b))
         for i in range(args.warmup):
@@ -771,7 +999,8 @@ def main():
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--gt", type=int, default=8192)
-    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (and build parity) legs")
+    ap.add_argument("--no-ref", action="store_true", help="skip the reference-kernel leg")
     ap.add_argument("--fixed", default="", help="branches,queue,stop_eps: skip the calibration")
     ap.add_argument("--build-only", action="store_true", help="time the graph build instead of the search")
     ap.add_argument("--batch-sweep", action="store_true", help="QPS and latency across the C3 batch sizes")

@@ -10,7 +10,9 @@
  * Each entry point names the reference interface it replaces (paths inside
  * geniussyn/SWANN).  The reference binds its kernels through pybind
  * (swann/csrc/local_search.cu:950-955) and torch (swann/build.py); a
- * maintainer binds these through ctypes instead.
+ * maintainer binds these through ctypes instead: swann_b200/_lib.py declares
+ * every signature below, and swann_b200/refext.py keeps the reference's own
+ * pybind argument lists on top of them.
  */
 #ifndef SWANN_B200_H
 #define SWANN_B200_H
@@ -89,8 +91,9 @@ SWB_API int swb_search_init(const void* X, int x_dtype, int64_t n, int dim,
  *            per-node scale |x - mu|_1 / dim; code_mu [dim] the corpus mean.
  *            A neighbour whose estimated distance exceeds the step's expansion
  *            limit by more than code_margin is not read.  NULL = off.
- *   status   optional int32 device word; a device-side wait that runs out sets
- *            it to SWB_ERR_TIMEOUT (never set in normal operation) */
+ *   status   optional int32 device word, kept for symmetry with the build
+ *            calls: the search kernels have no device-side waits, so they
+ *            never write it (a caller may pass NULL) */
 SWB_API int swb_search_advance(const void* X, int x_dtype, int64_t n, int dim,
                        const int32_t* G, int D, const float* Qv,
                        int32_t* ids, float* dist, uint8_t* expanded, uint8_t* lineage,
@@ -136,7 +139,8 @@ SWB_API int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int
  *   qdone    [Q] int32, cleared by swb_search_prepare
  *   out_ids/out_dist [Q, k] (out)
  *   ids/dist/expanded/lineage/counters: optional outputs of the final branch
- *   states (NULL to skip), shapes as in swb_search_init */
+ *   states (NULL to skip), shapes as in swb_search_init
+ *   status: as in swb_search_advance (never written; NULL is fine) */
 SWB_API int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim,
                      const int32_t* G, int D, const float* Qv, const int32_t* seeds,
                      int Q, int J, int V, int k, int L, int B,
@@ -170,7 +174,10 @@ SWB_API int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim,
  *   - One seed per branch (seeds [Q, J]), POLICY_BEST, no stall or crowd
  *     rules; shared_cache / shared_bound / exclusive / elide_visited as in
  *     swb_search_fused; Hc is the per-query table size (a power of two).
- *   - status (optional) receives SWB_ERR_TIMEOUT if a device wait gave up. */
+ *   - status is accepted for symmetry and never written (the search has no
+ *     device-side waits); NULL is fine.
+ *   - Q <= 65535, D <= SWB_MAX_DEGREE, L <= SWB_MAX_QUEUE and a visited table
+ *     of at most 2^30 slots (B * D bounded) are checked before any sizing. */
 #define SWB_STATIC_SCRATCH_BYTES (32u << 20)
 SWB_API int swb_search_fused_static(const void* X, int x_dtype, int64_t n, int dim,
                             const int32_t* G, int D, const float* Qv, const int32_t* seeds,

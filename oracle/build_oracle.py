@@ -6,10 +6,13 @@ the working tree:
 * ``oracle/liboracle.so`` -- the C restatement in ``swann_oracle.c``.
 * ``oracle/_ref/swann_ref_ls*.so`` -- the reference's own search kernels
   (``swann/csrc/local_search.cu`` of geniussyn/SWANN), compiled unmodified for
-  sm_100a from the read-only reference tree when that tree is present.  It is a
-  torch extension with the reference's pybind entry points; tests load it only
-  as a checker.  The reference JIT-compiles the same file with
-  ``-O3 -lineinfo -fmad=false`` (swann/_engine.py:42-63); the flags are kept.
+  sm_100a.  The source is taken from the reference project named by the
+  ``SWANN_REFERENCE`` environment variable (its root directory), else from the
+  reference package installed under ``baseline/_ref`` (``baseline/install.sh``).
+  It is a torch extension with the reference's pybind entry points; tests and
+  the bench's baseline legs load it only as a checker or baseline.  The
+  reference JIT-compiles the same file with ``-O3 -lineinfo -fmad=false``
+  (swann/_engine.py:42-63); the flags are kept.
 
 Usage:  python oracle/build_oracle.py [--ref]
 """
@@ -25,8 +28,23 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_DIR = HERE / "_ref"
-REF_SRC = Path("/root/reference/swann/csrc/local_search.cu")
 REF_NAME = "swann_ref_ls"
+INSTALLED_REF = HERE.parent / "baseline" / "_ref"
+
+
+def reference_source() -> Path | None:
+    """swann/csrc/local_search.cu of the reference: under $SWANN_REFERENCE when
+    set, else in the installed copy under baseline/_ref; None when neither
+    exists."""
+    roots = []
+    if os.environ.get("SWANN_REFERENCE"):
+        roots.append(Path(os.environ["SWANN_REFERENCE"]))
+    roots.append(INSTALLED_REF)
+    for r in roots:
+        src = r / "swann" / "csrc" / "local_search.cu"
+        if src.exists():
+            return src
+    return None
 
 
 def _newer(out: Path, *srcs: Path) -> bool:
@@ -49,10 +67,11 @@ def ref_so_path() -> Path:
 
 def build_ref(force: bool = False) -> Path | None:
     """Compile the reference's kernel file for sm_100a (only where it exists)."""
-    if not REF_SRC.exists():
+    src = reference_source()
+    if src is None:
         return ref_so_path() if ref_so_path().exists() else None
     out = ref_so_path()
-    if not force and _newer(out, REF_SRC):
+    if not force and _newer(out, src):
         return out
     import torch
     from torch.utils.cpp_extension import include_paths, library_paths
@@ -69,7 +88,7 @@ def build_ref(force: bool = False) -> Path | None:
             else library_paths(cuda=True):
         libs += ["-L", p]
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
-    cmd = [nvcc, str(REF_SRC), "-o", str(out), "-shared", "-Xcompiler", "-fPIC",
+    cmd = [nvcc, str(src), "-o", str(out), "-shared", "-Xcompiler", "-fPIC",
            "-std=c++17", "-O3", "-lineinfo", "-fmad=false", "--expt-relaxed-constexpr",
            "-gencode", "arch=compute_100a,code=sm_100a",
            f"-DTORCH_EXTENSION_NAME={REF_NAME}", "-DTORCH_API_INCLUDE_EXTENSION_H",

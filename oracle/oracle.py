@@ -57,12 +57,12 @@ def _declare(L):
     L.or_team_distance.argtypes = [vp, vp, i32, i32, i32, i32]
     L.or_branch_run.restype = i32
     L.or_branch_run.argtypes = [vp, i32, vp, i32, vp, vp, i32, i32, i32, i32, i32, i32,
-                                i32, f32, i32, i32, vp, vp, vp, vp, vp]
+                                i32, f32, i32, i32, f32, i32, vp, vp, vp, vp, vp]
     L.or_merge_branches.restype = None
     L.or_merge_branches.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp]
     L.or_search.restype = i32
     L.or_search.argtypes = [vp, i64, i32, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32,
-                            i32, i32, i32, i32, f32, i32, i32, i32, i32, i32, i32, vp, vp, vp]
+                            i32, i32, i32, i32, f32, i32, i32, i32, i32, i32, i32, f32, i32, vp, vp, vp]
     L.or_knn_candidates.restype = i32
     L.or_knn_candidates.argtypes = [vp, i64, i32, i32, i32, i64, i64, i32, vp, vp, vp]
     L.or_robust_prune.restype = i32
@@ -109,23 +109,26 @@ def team_distance(q, x, metric=METRIC_IP, team=32, vec=4) -> np.float32:
 
 
 def branch_run(X, G, q, seeds, L=16, B=16, metric=METRIC_IP, team=32, vec=None,
-               policy=POLICY_BEST, stop_eps=-1.0, kstop=10, delta=None):
-    """One branch, init + advance(delta or B).  Returns dict of L-slot arrays."""
+               policy=POLICY_BEST, stop_eps=-1.0, kstop=10, delta=None, stall_patience=0, crowd_frac=0.0):
+    """One branch, init + advance(delta or B).  Returns dict of L-slot arrays.
+    stall_patience / crowd_frac: the kernel's stall and crowd rules
+    (swann/csrc/local_search.cu:659-682), 0 = off."""
     vec = default_vec(X) if vec is None else vec
     X, G, q = _f32(X), _i32(G), _f32(q)
     seeds = _i32(np.atleast_1d(seeds))
     ids = np.empty(L, np.int32); dist = np.empty(L, np.float32)
     expd = np.empty(L, np.uint8); lin = np.empty(L, np.uint8); ctr = np.empty(NCTR, np.int32)
     lib().or_branch_run(_p(X), X.shape[1], _p(G), G.shape[1], _p(q), _p(seeds), seeds.shape[0],
-                        L, B, metric, team, vec, policy, float(stop_eps), kstop,
-                        B if delta is None else delta, _p(ids), _p(dist), _p(expd), _p(lin), _p(ctr))
+                        L, B, metric, team, vec, policy, float(stop_eps), kstop, int(stall_patience),
+                        float(crowd_frac), B if delta is None else delta, _p(ids), _p(dist), _p(expd), _p(lin),
+                        _p(ctr))
     return dict(ids=ids, dist=dist, expanded=expd, lineage=lin, counters=ctr)
 
 
 def search(X, G, Q, seeds, k=10, L=16, B=16, metric=METRIC_IP, team=32, vec=None,
            policy=POLICY_BEST, stop_eps=-1.0, kstop=None, shared_cache=False,
            shared_bound=False, exclusive=False, elide_visited=False, threads=0,
-           counters=False):
+           counters=False, stall_patience=0, crowd_frac=0.0):
     """seeds [nq, J] or [nq, J, V].  Returns (ids [nq,k], dist [nq,k][, ctr])."""
     vec = default_vec(X) if vec is None else vec
     X, G, Q = _f32(X), _i32(G), _f32(Q)
@@ -139,7 +142,7 @@ def search(X, G, Q, seeds, k=10, L=16, B=16, metric=METRIC_IP, team=32, vec=None
     lib().or_search(_p(X), X.shape[0], X.shape[1], _p(G), G.shape[1], _p(Q), nq, _p(seeds), J, V,
                     k, L, B, metric, team, vec, policy, float(stop_eps), kstop,
                     int(shared_cache), int(shared_bound), int(exclusive), int(elide_visited),
-                    int(threads), _p(ids), _p(dist), _p(ctr))
+                    int(stall_patience), float(crowd_frac), int(threads), _p(ids), _p(dist), _p(ctr))
     return (ids, dist, ctr) if counters else (ids, dist)
 
 

@@ -14,6 +14,8 @@
  *                                     shared-table / bound / exclusive modes
  *                                     that _refcpu does not model
  *           swann/csrc/local_search.cu:637-650  merge-path tie rule
+ *           swann/csrc/local_search.cu:659-682  crowd and stall rules (the
+ *                                     kernel's only; _refcpu has neither)
  *           swann/csrc/local_search.cu:863-919  merge of branch results
  *   build   swann/build.py:14-43      pairwise + knn_candidates
  *           swann/build.py:48-91      robust_prune
@@ -164,6 +166,8 @@ typedef struct {
     /* knobs */
     int L, B, V, policy, kstop;
     float stop_eps;
+    int stall_patience; /* stop after this many steps without a better k-th best; 0 = off */
+    float crowd_frac;   /* retire a lineage after two steps this crowded; 0 = off */
     int use_visited;   /* H > 1 in the kernel */
     /* state */
     entry_t* queue;    /* L slots, empty = (-1, FLT_MAX, 1, 0) */
@@ -172,6 +176,9 @@ typedef struct {
     iset_t visited;
     int ctr[OR_NCTR];
     uint32_t retired[8];
+    /* per-advance-call rule state (local_search.cu:396-415: reset every call) */
+    float best_k;
+    int stall, crowd_run;
     int done;
 } branch_t;
 
@@ -189,6 +196,9 @@ static void branch_alloc(branch_t* b) {
     if (b->use_visited) iset_init(&b->visited, (int64_t)b->V + (int64_t)b->B * b->D + 1, 0);
     memset(b->ctr, 0, sizeof(b->ctr));
     memset(b->retired, 0, sizeof(b->retired));
+    b->best_k = FLT_MAX;
+    b->stall = 0;
+    b->crowd_run = 0;
     b->done = 0;
 }
 static void branch_free(branch_t* b) {
@@ -279,15 +289,18 @@ static int branch_step(branch_t* b, qshared_t* sh) {
     const uint8_t plin = b->queue[slot].l;
     b->ctr[0] += 1;
 
-    /* expand p, candidates in G's slot order */
-    int nc = 0;
+    /* expand p, candidates in G's slot order; nbr counts the neighbours and
+     * cov those already covered -- in this branch's visited set, or claimed
+     * and scored by another branch (local_search.cu:533-585) */
+    int nc = 0, nbr = 0, cov = 0;
     for (int s = 0; s < b->D; ++s) {
         const int v = b->G[(size_t)p * b->D + s];
         if (v < 0) continue;
+        ++nbr;
         if (b->use_visited) {
             int found;
             iset_insert(&b->visited, v, &found);
-            if (found) continue;
+            if (found) { ++cov; continue; }
         }
         float dv = FLT_MAX;
         int have = 0, taken = 0;
@@ -311,7 +324,7 @@ static int branch_step(branch_t* b, qshared_t* sh) {
             dv = or_team_distance(b->q, b->X + (size_t)v * b->d, b->d, b->metric, b->team, b->vec);
             b->ctr[1] += 1;
         }
-        if (taken) continue;
+        if (taken) { ++cov; continue; }
         b->cand[nc].id = v;
         b->cand[nc].d = dv;
         b->cand[nc].e = 0;
@@ -346,6 +359,31 @@ static int branch_step(branch_t* b, qshared_t* sh) {
     memcpy(b->queue, b->merged, sizeof(entry_t) * (size_t)L);
     if (sh && sh->shared_bound && kr > 0 && b->queue[kr - 1].id >= 0 && b->queue[kr - 1].d < sh->bound)
         sh->bound = b->queue[kr - 1].d;
+    /* crowding (local_search.cu:659-671): a lineage whose expansions land on
+     * covered ground two steps in a row is retired */
+    if (b->crowd_frac > 0.0f) {
+        const float cv = (nbr > 0) ? ((float)cov / (float)nbr) : 0.0f;
+        if (cv >= b->crowd_frac) {
+            if (++b->crowd_run >= 2) {
+                retired_set(b, (unsigned)plin);
+                b->ctr[7] += 1;
+                b->crowd_run = 0;
+            }
+        } else {
+            b->crowd_run = 0;
+        }
+    }
+    /* stalling (local_search.cu:672-682): stop once the k-th best has not
+     * improved for stall_patience steps */
+    if (b->stall_patience > 0) {
+        const float bk = (kr > 0 && b->queue[kr - 1].id >= 0) ? b->queue[kr - 1].d : FLT_MAX;
+        if (bk < b->best_k) { b->best_k = bk; b->stall = 0; }
+        else b->stall += 1;
+        if (b->stall >= b->stall_patience) {
+            b->ctr[6] = 1;
+            return 0;
+        }
+    }
     return 1;
 }
 
@@ -363,13 +401,14 @@ static void branch_export(const branch_t* b, int* ids, float* dist, uint8_t* exp
  * for one branch seeded with V entries.  Outputs are the kernel's L slots. */
 int or_branch_run(const float* X, int d, const int* G, int D, const float* q,
                   const int* seeds, int V, int L, int B, int metric, int team, int vec,
-                  int policy, float stop_eps, int kstop, int delta,
+                  int policy, float stop_eps, int kstop, int stall_patience, float crowd_frac, int delta,
                   int* ids, float* dist, uint8_t* expd, uint8_t* lin, int* ctr) {
     branch_t b;
     memset(&b, 0, sizeof(b));
     b.X = X; b.d = d; b.G = G; b.D = D; b.q = q;
     b.metric = metric; b.team = team; b.vec = vec;
     b.L = L; b.B = B; b.V = V; b.policy = policy; b.kstop = kstop; b.stop_eps = stop_eps;
+    b.stall_patience = stall_patience; b.crowd_frac = crowd_frac;
     b.use_visited = 1;
     branch_alloc(&b);
     branch_init(&b, seeds);
@@ -440,7 +479,7 @@ int or_search(const float* X, int64_t n, int d, const int* G, int D,
               const float* Q, int nq, const int* seeds, int J, int V,
               int k, int L, int B, int metric, int team, int vec, int policy,
               float stop_eps, int kstop, int shared_cache, int shared_bound,
-              int exclusive, int elide_visited, int nthreads,
+              int exclusive, int elide_visited, int stall_patience, float crowd_frac, int nthreads,
               int* out_ids, float* out_dist, int* out_ctr) {
     (void)n;
     const int kk = k < L ? k : L;
@@ -466,6 +505,7 @@ int or_search(const float* X, int64_t n, int d, const int* G, int D,
             b->X = X; b->d = d; b->G = G; b->D = D; b->q = Q + (size_t)qi * d;
             b->metric = metric; b->team = team; b->vec = vec;
             b->L = L; b->B = B; b->V = V; b->policy = policy; b->kstop = kstop; b->stop_eps = stop_eps;
+            b->stall_patience = stall_patience; b->crowd_frac = crowd_frac;
             b->use_visited = !elide;
             branch_alloc(b);
             branch_init(b, seeds + ((size_t)qi * J + j) * V);

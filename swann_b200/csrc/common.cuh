@@ -1,9 +1,6 @@
-// common.cuh -- device helpers shared by the search and build kernels (sm_100a).
-//
-// Bulk copies: cp.async.bulk (the TMA engine's non-tensor form) moves whole
-// corpus rows from HBM into shared memory and signals an mbarrier with the byte
-// count; one lane issues a row, so a warp keeps many rows in flight without
-// spending registers on them.  Every wait on an mbarrier is bounded.
+// common.cuh -- device helpers shared by the search and build kernels (sm_100a):
+// mbarrier primitives (every wait bounded), the (distance, id) order, and the
+// reference's distance arithmetic over 16-byte row chunks.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -43,24 +40,9 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-// orders this thread's generic-proxy shared-memory accesses before later
-// async-proxy (bulk copy) accesses to the same memory
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
-}
-
-// global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

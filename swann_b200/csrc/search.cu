@@ -1314,17 +1314,32 @@ int static_scratch_ptr(void** out) {
 
 }  // namespace
 
+// Per-branch visited-table slots of the fixed-scratch search: 1 when elided,
+// else the next power of two >= 2 (1 + B D), computed in 64 bits; 0 when the
+// knobs are out of range (B or D not positive, D beyond the kernel's limit, or
+// a table beyond 2^30 slots), which every caller turns into a rejection.
+int64_t static_visited_slots(int B, int D, bool elide) {
+    if (B < 1 || D < 1 || D > MAXD) return 0;
+    if (elide) return 1;
+    const int64_t want = 2 * (1 + (int64_t)B * (int64_t)D);
+    if (want > ((int64_t)1 << 30)) return 0;
+    int64_t p = 1;
+    while (p < want) p <<= 1;
+    return p;
+}
+
 extern "C" uint64_t swb_search_static_bytes(int Q, int J, int k, int L, int B, int D, int Hc, int shared_cache,
                                             int exclusive, int elide_visited) {
+    if (Q < 0 || J < 0 || k < 1 || L < 1 || Hc < 0) return UINT64_MAX;
     const int kk = k < L ? k : L;
     const bool table = shared_cache && J > 1 && Hc > 0;
     const bool elide = elide_visited && exclusive && table;
-    const int H = elide ? 1 : pow2_at_least(2 * (1 + B * D));
+    const int64_t H = static_visited_slots(B, D, elide);
+    if (H == 0) return UINT64_MAX;
     size_t b = 0;
     b += align256((size_t)Q * 4);                           // completion counters
     b += align256((size_t)Q * 4);                           // bounds
     b += align256((size_t)Q * J * kk * 4) * 2;              // per-branch ids, distances
-    b += align256((size_t)4);                               // status word
     if (table) b += align256((size_t)Q * Hc * 8);           // distance tables
     if (H > 1) b += align256((size_t)Q * J * H * 4);        // visited tables
     return b;
@@ -1338,7 +1353,15 @@ extern "C" int swb_search_fused_static(const void* X, int x_dtype, int64_t n, in
     if (Q <= 0 || J <= 0) return SWB_OK;
     if (Hc > 0 && !pow2(Hc)) return abi::fail(SWB_ERR_ARG, "table size must be a power of two");
     if (k < 1 || L < 1 || B < 1 || D < 1) return abi::fail(SWB_ERR_ARG, "k, L, B and D must be positive");
+    if (D > MAXD) return abi::fail(SWB_ERR_ARG, "graph degree must be 1..%d", MAXD);
+    if (L > MAXL) return abi::fail(SWB_ERR_ARG, "L exceeds MAXL (%d)", MAXL);
+    if (Q > SWB_MAX_BATCH)
+        return abi::fail(SWB_ERR_BATCH, "batch of %d queries exceeds the 65535 one call allows; split the batch", Q);
+    if (J > 4 * MAXD) return abi::fail(SWB_ERR_ARG, "at most %d branches per query", 4 * MAXD);
     const uint64_t need = swb_search_static_bytes(Q, J, k, L, B, D, Hc, shared_cache, exclusive, elide_visited);
+    if (need == UINT64_MAX)
+        return abi::fail(SWB_ERR_ARG, "the budget B = %d with degree D = %d needs a visited table beyond 2^30 slots",
+                         B, D);
     if (need > kStaticScratchBytes)
         return abi::fail(SWB_ERR_ARG,
                          "this search needs %llu bytes of scratch; the library's fixed scratch holds %llu. "
@@ -1350,13 +1373,12 @@ extern "C" int swb_search_fused_static(const void* X, int x_dtype, int64_t n, in
     const int kk = k < L ? k : L;
     const bool table = shared_cache && J > 1 && Hc > 0;
     const bool elide = elide_visited && exclusive && table;
-    const int H = elide ? 1 : pow2_at_least(2 * (1 + B * D));
+    const int H = (int)static_visited_slots(B, D, elide);   // in range: the size check above passed
     char* p = static_cast<char*>(base);
     int32_t* qdone = reinterpret_cast<int32_t*>(p); p += align256((size_t)Q * 4);
     float* bound = reinterpret_cast<float*>(p); p += align256((size_t)Q * 4);
     int32_t* bids = reinterpret_cast<int32_t*>(p); p += align256((size_t)Q * J * kk * 4);
     float* bdist = reinterpret_cast<float*>(p); p += align256((size_t)Q * J * kk * 4);
-    int32_t* own_status = reinterpret_cast<int32_t*>(p); p += align256((size_t)4);
     uint64_t* cache = nullptr;
     if (table) { cache = reinterpret_cast<uint64_t*>(p); p += align256((size_t)Q * Hc * 8); }
     int32_t* visited = nullptr;
@@ -1368,9 +1390,8 @@ extern "C" int swb_search_fused_static(const void* X, int x_dtype, int64_t n, in
     rc = swb_search_prepare(Q, table ? cache : nullptr, table ? Hc : 0, shared_bound && J > 1 ? bound : nullptr,
                             qdone, stream);
     if (rc) return rc;
-    int32_t* stat = status ? status : own_status;
     return swb_search_fused(X, x_dtype, n, dim, G, D, Qv, seeds, Q, J, 1, k, L, B, metric, team, 0, stop_eps, k,
                             visited, H, cache, table ? Hc : 0, shared_bound && J > 1 ? bound : nullptr,
                             table ? exclusive : 0, 0, 0.f, bids, bdist, qdone, out_ids, out_dist, nullptr, nullptr,
-                            nullptr, nullptr, nullptr, stat, st);
+                            nullptr, nullptr, nullptr, status, st);
 }

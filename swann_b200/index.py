@@ -22,7 +22,6 @@ import numpy as np
 import torch
 
 from . import _engine as E
-from . import _lib as N
 from . import _select as S
 
 METRICS = {"ip": E.METRIC_IP, "l2": E.METRIC_L2}
@@ -65,7 +64,9 @@ class _Replica:
         self.X = X if X.device == dev else X.to(dev)
         self.G = G if G.device == dev else G.to(dev)
         self.catalogue = catalogue if catalogue.device == dev else catalogue.to(dev)
-        self.cat_rows = S.pool_vectors(self.X.float(), self.catalogue)
+        # gather the P catalogue rows first, then widen them: no fp32 copy of
+        # the whole corpus (the values are the same either way)
+        self.cat_rows = S.pool_vectors(self.X, self.catalogue).float()
 
 
 class Index:
@@ -109,17 +110,58 @@ class Index:
         self._tour = _catalogue_tour(self._cat, self._m) if self.locality else None
         for r in self._replicas:
             r.tour = None if self._tour is None else self._tour.to(r.dev)
-        # Slots of each query's distance table.  None: the reference's sizing
-        # (swann/_engine.py:186-198).  The table only ever holds the nodes a
-        # query's branches score (a few thousand); any power of two that keeps
-        # its load low leaves every result unchanged and clears faster.
+        # Slots of each query's distance table.  A power of two fixes it.
+        # None (the default) sizes it from what the queries claim: the first
+        # search of a configuration uses the reference's sizing
+        # (swann/_engine.py:186-198, 131072 slots at 32 branches), and every
+        # search records the most slots any of its queries claimed; later
+        # searches of that configuration use TABLE_HEADROOM times that, a
+        # power of two.  The table only ever holds the nodes a query's
+        # branches score (a few thousand), and a probe run that finds no free
+        # slot scores the row uncached, so the size moves the work and the
+        # clearing cost, never what a result may be.
         if table_slots is not None and (table_slots < 2 or table_slots & (table_slots - 1)):
             raise ValueError("table_slots must be a power of two")
         self.table_slots = table_slots
+        self._claims = {}        # (branches, budget, queue, stop_eps, degree) -> most claims per query
+        self._pending = []       # claim counts still on their way to the host (overflow guard off)
 
     @property
     def devices(self):
         return [r.dev for r in self._replicas]
+
+    # -- per-query table size ------------------------------------------------
+    def table_slots_for(self, branches, budget, queue, stop_eps, degree) -> int:
+        """Slots of the per-query table a search with these knobs runs with."""
+        if self.table_slots is not None:
+            return self.table_slots
+        self._fold_pending()
+        ref = E.cache_size(branches, budget, degree)
+        seen = self._claims.get(_claims_key(branches, budget, queue, stop_eps, degree))
+        if seen is None:
+            return ref
+        return min(ref, max(TABLE_MIN, E.next_pow2(int(TABLE_HEADROOM * seen))))
+
+    def _note_claims(self, key, claims, host_value=None):
+        """Record the most slots a query of one launch claimed: `host_value`
+        when the caller already read it, else read later without a stall."""
+        if host_value is not None:
+            self._claims[key] = max(self._claims.get(key, 0), int(host_value))
+            return
+        buf = torch.empty((1,), dtype=torch.int64, pin_memory=True)
+        buf.copy_(claims.reshape(1), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(claims.device))
+        self._pending.append((key, buf, ev))
+
+    def _fold_pending(self):
+        keep = []
+        for key, buf, ev in self._pending:
+            if ev.query():
+                self._claims[key] = max(self._claims.get(key, 0), int(buf[0]))
+            else:
+                keep.append((key, buf, ev))
+        self._pending = keep
 
     # -- construction ----------------------------------------------------
     @classmethod
@@ -157,7 +199,7 @@ class Index:
             if b <= a:
                 continue
             with torch.cuda.device(r.dev):
-                Hc = self.table_slots or E.cache_size(cfg.branches, cfg.budget, r.G.shape[1])
+                Hc = self.table_slots_for(cfg.branches, cfg.budget, cfg.queue, cfg.stop_eps, r.G.shape[1])
                 if host is not None and b - a > COPY_CHUNK:
                     # Host queries: copied chunk by chunk on a side stream; each
                     # chunk's seeds are selected as it lands (the copies overlap
@@ -189,12 +231,20 @@ class Index:
                     src = host if host is not None else queries
                     Qd = src[a:b].to(r.dev, non_blocking=True).float().contiguous()
                     self._search_part(r, Qd, k, cfg, Hc, outs, checks)
-        if E._OVERFLOW_GUARD:
-            for ctr, status in checks:
-                if ctr is not None and int(ctr[..., 2].sum()) != 0:
-                    raise RuntimeError("visited table overflowed: raise the budget used for sizing")
-                if int(status[0]) != 0:
-                    raise N.SwannError(int(status[0]), "a device-side wait timed out during the search")
+        key_of = lambda r: _claims_key(cfg.branches, cfg.budget, cfg.queue, cfg.stop_eps, r.G.shape[1])  # noqa: E731
+        overflow = 0
+        for r, ctr in checks:
+            # the most table slots one query claimed (its branches' claims plus
+            # their seeds), and the visited-table overflow count
+            claims = (ctr[..., 5].to(torch.int64).sum(1) + ctr.shape[1]).max()
+            if E._OVERFLOW_GUARD:
+                fails, most = torch.stack([ctr[..., 2].to(torch.int64).sum(), claims]).tolist()
+                overflow += fails
+                self._note_claims(key_of(r), claims, host_value=most)
+            else:
+                self._note_claims(key_of(r), claims)
+        if overflow:
+            raise RuntimeError("visited table overflowed: raise the budget used for sizing")
         dev0 = reps[0].dev
         ids = torch.cat([o[0].to(dev0) for o in outs]) if outs else torch.empty((0, k), dtype=torch.int32)
         dist = torch.cat([o[1].to(dev0) for o in outs]) if outs else torch.empty((0, k))
@@ -204,7 +254,7 @@ class Index:
         """Seed selection and the fused search of one device-resident block of
         queries, in table-budget sized launches (and locality order, see
         `locality`); appends (ids, dist) in input order to `outs` and each
-        launch's (counters, status) to `checks`.  `ent`: the seeds' catalogue
+        launch's (replica, counters) to `checks`.  `ent`: the seeds' catalogue
         indices when already selected."""
         nq = Qd.shape[0]
         step = max(1, min(nq, TABLE_BUDGET // (8 * Hc)))
@@ -229,10 +279,10 @@ class Index:
             c1 = min(nq, c0 + step)
             if prep is not None:
                 torch.cuda.current_stream(r.dev).wait_event(prep)
-            ids, dist, ctr, status = _search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc,
-                                                    prepared=prep is not None)
+            ids, dist, ctr, _ = _search_device(r, Qd[c0:c1], seeds[c0:c1], k, cfg, self._m, Hc,
+                                               prepared=prep is not None)
             part.append((ids, dist))
-            checks.append((ctr, status))
+            checks.append((r, ctr))
         ids = torch.cat([p[0] for p in part]) if len(part) > 1 else part[0][0]
         dist = torch.cat([p[1] for p in part]) if len(part) > 1 else part[0][1]
         if order is not None:
@@ -289,6 +339,15 @@ class Index:
 
 # catalogues up to this size get a locality tour (an O(P^2) pass, once)
 TOUR_MAX = 16384
+# measured-claims table sizing: slots = TABLE_HEADROOM x the most slots one query
+# claimed so far, a power of two, at least TABLE_MIN (load <= 67% for the
+# busiest query seen, ~15% for a typical one at C3)
+TABLE_HEADROOM = 1.5
+TABLE_MIN = 4096
+
+
+def _claims_key(branches, budget, queue, stop_eps, degree):
+    return (int(branches), int(budget), int(queue), float(stop_eps), int(degree))
 
 
 def _catalogue_tour(cat_rows, metric):

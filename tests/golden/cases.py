@@ -106,3 +106,23 @@ def merge_inputs(Q=7, J=5, kk=10, seed=3):
                 ids[q, j, kk - nempty:] = -1
                 dist[q, j, kk - nempty:] = np.finfo(np.float32).max
     return ids, dist
+
+
+def aniso_mixture(n, d, clusters, seed, nq=0, qseed=None):
+    """BASELINE config 3's corpus model at any size: `clusters` centres
+    N(0, 1)^d, per-cluster per-dimension scales exp(U(ln 0.1, ln 1)), rows
+    c + s * z, L2-normalised.  Returns (X float32 [n, d], Q float32 [nq, d]),
+    the queries drawn from the same mixture with their own seed."""
+    g = np.random.default_rng(seed)
+    centres = g.standard_normal((clusters, d), dtype=np.float32)
+    scales = np.exp(np.log(0.1) + (np.log(1.0) - np.log(0.1)) * g.random((clusters, d), dtype=np.float32))
+
+    def draw(m, rng):
+        c = rng.integers(0, clusters, m)
+        x = centres[c] + scales[c] * rng.standard_normal((m, d), dtype=np.float32)
+        x /= np.linalg.norm(x, axis=1, keepdims=True)
+        return np.ascontiguousarray(x, dtype=np.float32)
+
+    X = draw(n, np.random.default_rng(seed + 1))
+    Q = draw(nq, np.random.default_rng(seed + 2 if qseed is None else qseed)) if nq else None
+    return X, Q

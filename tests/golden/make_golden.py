@@ -10,11 +10,12 @@ importable there; they do not travel to the GPU box).  Imports, read-only:
 
 and writes outputs (plus input digests) to tests/golden/*.npz.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--skip-c1]
+    python tests/golden/make_golden.py [--ref REFERENCE_ROOT] [--skip-c1]
 """
 from __future__ import annotations
 
 import argparse
+import os
 import functools
 import multiprocessing as mp
 import sys
@@ -225,9 +226,12 @@ def gen_c1(refpath):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("SWANN_REFERENCE"),
+                    help="root of the reference project (default: $SWANN_REFERENCE)")
     ap.add_argument("--skip-c1", action="store_true")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("name the reference project's root with --ref or $SWANN_REFERENCE")
     refcpu = _import_ref(a.ref)
     gen_distances(refcpu)
     gen_branches(refcpu)

@@ -4,13 +4,14 @@ candidates_from_graph, mutual_rank, robust_prune with per-node degrees and
 protected pairs, add_reverse with per-node degrees, fill_degree (all three
 rules, 64-row chunks so the chunk order matters) and enforce_min_in.
 
-    python tests/golden/make_offline_golden.py [--ref /root/reference]
+    python tests/golden/make_offline_golden.py [--ref REFERENCE_ROOT]
 
 Writes tests/golden/offline.npz.  Runs only where the reference is mounted.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import contextlib
 import io
 import sys
@@ -38,8 +39,11 @@ def test_graph(cand, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("SWANN_REFERENCE"),
+                    help="root of the reference project (default: $SWANN_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("name the reference project's root with --ref or $SWANN_REFERENCE")
     sys.path.insert(0, a.ref)
     import torch
     from offline import build_graph as R   # the reference's module, unmodified

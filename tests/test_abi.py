@@ -60,3 +60,46 @@ def test_argument_errors_need_no_gpu():
     assert rc == N.ERR_ARG
     with pytest.raises(ValueError):
         N.check(rc)
+
+
+def test_static_scratch_sizing_rejects_out_of_range_knobs():
+    """The no-allocation entry point sizes its scratch in 64 bits and rejects
+    knobs outside the kernels' limits before touching the GPU: a budget and
+    degree whose visited table would pass 2^30 slots, a degree beyond the
+    limit, a batch beyond 65535."""
+    L = N.lib()
+    assert L.swb_search_static_bytes(16, 8, 10, 12, 64, 64, 4096, 1, 2, 1) < (32 << 20)
+    assert L.swb_search_static_bytes(1, 1, 10, 12, 1 << 24, 128, 0, 0, 0, 0) == 2 ** 64 - 1
+    assert L.swb_search_static_bytes(1, 1, 10, 12, 64, 129, 0, 0, 0, 0) == 2 ** 64 - 1
+    args = dict(X=1 << 20, G=1 << 20, Q=1 << 20, S=1 << 20)
+    rc = L.swb_search_fused_static(args["X"], 0, 1000, 64, args["G"], 200, args["Q"], args["S"], 4, 4, 10, 12, 64,
+                                   0, 16, 0.05, 1, 1, 2, 1, 4096, 1 << 20, 1 << 20, None, None)
+    assert rc == N.ERR_ARG and b"degree" in L.swb_last_error()
+    rc = L.swb_search_fused_static(args["X"], 0, 1000, 64, args["G"], 64, args["Q"], args["S"], 4, 1, 10, 12,
+                                   1 << 24, 0, 16, 0.05, 0, 0, 0, 0, 0, 1 << 20, 1 << 20, None, None)
+    assert rc == N.ERR_ARG and b"2^30" in L.swb_last_error()
+    rc = L.swb_search_fused_static(args["X"], 0, 1000, 64, args["G"], 64, args["Q"], args["S"], 70000, 4, 10, 12,
+                                   64, 0, 16, 0.05, 1, 1, 2, 1, 4096, 1 << 20, 1 << 20, None, None)
+    assert rc == N.ERR_BATCH
+
+
+def test_refext_keeps_the_reference_signatures():
+    """swann_b200.refext exposes the reference's three pybind entry points
+    (swann/csrc/local_search.cu:950-955) with their argument lists, and its
+    argument errors are RuntimeErrors, as the reference's TORCH_CHECKs are."""
+    import inspect
+
+    import torch
+
+    from swann_b200 import refext
+    assert list(inspect.signature(refext.init_states).parameters) == [
+        "X", "Qv", "seeds", "ids", "dist", "expd", "lin", "visited", "counters", "metric", "team_size",
+        "cache_id", "cache_d", "bound"]
+    assert list(inspect.signature(refext.advance).parameters) == [
+        "X", "G", "Qv", "ids", "dist", "expd", "lin", "visited", "counters", "metric", "team_size", "delta",
+        "max_expansions", "policy", "V_in", "stop_eps", "kstop", "cache_id", "cache_d", "bound", "exclusive",
+        "stall_patience", "crowd_frac", "active", "codes", "alpha", "cmu", "code_margin"]
+    assert list(inspect.signature(refext.merge_branches).parameters) == ["bids", "bdist", "k"]
+    t = torch.zeros((2, 1, 4))
+    with pytest.raises(RuntimeError, match="X: contiguous cuda"):
+        refext.init_states(t, t, t, t, t, t, t, t, t, 0, 16, t, t, t)

@@ -14,54 +14,11 @@ import torch
 
 import cases
 from oracle import oracle as O
+from refcheck import DEV, ref_production, ref_run, same_state, to_gpu
 from swann_b200 import _engine as E
 
 pytestmark = pytest.mark.gpu
-DEV = "cuda"
 TEAMS = (4, 8, 16, 32)
-
-
-def to_gpu(X, G, Qv):
-    return (torch.from_numpy(np.ascontiguousarray(X)).to(DEV), torch.from_numpy(np.ascontiguousarray(G)).to(DEV),
-            torch.from_numpy(np.ascontiguousarray(Qv)).to(DEV))
-
-
-def ref_run(Xg, Gg, Qg, seeds, L, B, metric, team, policy=0, stop_eps=-1.0, kstop=10, V=None):
-    """The reference's own init_states + advance, deterministic mode."""
-    R = O.ref_kernels()
-    if R is None:
-        return None
-    seeds = seeds.to(DEV, torch.int32).contiguous()
-    if seeds.dim() == 2:
-        seeds = seeds.unsqueeze(-1).contiguous()
-    Q, J, V = seeds.shape
-    H = E.visited_size(B, Gg.shape[1])
-    ids = torch.empty((Q, J, L), dtype=torch.int32, device=DEV)
-    dist = torch.empty((Q, J, L), dtype=torch.float32, device=DEV)
-    expd = torch.empty((Q, J, L), dtype=torch.uint8, device=DEV)
-    lin = torch.empty((Q, J, L), dtype=torch.uint8, device=DEV)
-    vis = torch.empty((Q, J, H), dtype=torch.int32, device=DEV)
-    ctr = torch.empty((Q, J, 10), dtype=torch.int32, device=DEV)
-    ei = torch.empty((0, 0), dtype=torch.int32, device=DEV)
-    ef = torch.empty((0, 0), dtype=torch.float32, device=DEV)
-    eb = torch.empty((0,), dtype=torch.float32, device=DEV)
-    R.init_states(Xg, Qg, seeds, ids, dist, expd, lin, vis, ctr, metric, team, ei, ef, eb)
-    e0i = torch.empty(0, dtype=torch.int32, device=DEV)
-    e0f = torch.empty(0, dtype=torch.float32, device=DEV)
-    R.advance(Xg, Gg, Qg, ids, dist, expd, lin, vis, ctr, metric, team, B, B, policy, V, float(stop_eps), kstop,
-              ei, ef, eb, 0, 0, 0.0, e0i, e0i, e0f, e0f, 0.0)
-    torch.cuda.synchronize()
-    return ids, dist, expd, lin, ctr
-
-
-def same_state(st, ref):
-    ids, dist, expd, lin, ctr = ref
-    assert torch.equal(st.ids, ids)
-    assert torch.equal(st.dist.view(torch.int32), dist.view(torch.int32))
-    assert torch.equal(st.expanded, expd)
-    assert torch.equal(st.lineage, lin)
-    for c in (0, 1, 2, 3, 8, 9):
-        assert torch.equal(st.counters[..., c], ctr[..., c]), f"counter {c}"
 
 
 def test_cpu_gpu_exact():
@@ -437,28 +394,56 @@ def test_production_mode_matches_reference_statistically():
     ex = ((Q[:, None, :].astype(np.float64) - X[np.maximum(gi, 0)].astype(np.float64)) ** 2).sum(-1)
     rel = np.abs(dist.cpu().numpy().astype(np.float64) - ex) / np.maximum(ex, 1e-30)
     assert rel[ok].max() <= 1e-5
-    R = O.ref_kernels()
-    if R is None:
+    ref = ref_production(Xg, Gg, Qg, seeds, k=10, L=12, B=64, metric=1, team=16, stop_eps=0.05)
+    if ref is None:
         pytest.skip("reference kernels not built")
-    # the reference's production path (swann/_engine.py:219-278 with the
-    # Index.search flags), on the same seeds
-    Qn, J = seeds.shape
-    Hc = E.cache_size(J, 64, G.shape[1])
-    ids_r = torch.empty((Qn, J, 12), dtype=torch.int32, device=DEV)
-    dist_r = torch.empty((Qn, J, 12), dtype=torch.float32, device=DEV)
-    e_r = torch.empty((Qn, J, 12), dtype=torch.uint8, device=DEV)
-    l_r = torch.empty((Qn, J, 12), dtype=torch.uint8, device=DEV)
-    vis = torch.empty((Qn, J, 1), dtype=torch.int32, device=DEV)
-    ctr = torch.empty((Qn, J, 10), dtype=torch.int32, device=DEV)
-    cid = torch.empty((Qn, Hc), dtype=torch.int32, device=DEV)
-    cdd = torch.empty((Qn, Hc), dtype=torch.float32, device=DEV)
-    bnd = torch.empty((Qn,), dtype=torch.float32, device=DEV)
-    s3 = seeds.unsqueeze(-1).contiguous()
-    R.init_states(Xg, Qg, s3, ids_r, dist_r, e_r, l_r, vis, ctr, 1, 16, cid, cdd, bnd)
-    e0 = torch.empty(0, dtype=torch.int32, device=DEV)
-    e0f = torch.empty(0, dtype=torch.float32, device=DEV)
-    R.advance(Xg, Gg, Qg, ids_r, dist_r, e_r, l_r, vis, ctr, 1, 16, 64, 64, 0, 1, 0.05, 10, cid, cdd, bnd, 1,
-              0, 0.0, e0, e0, e0f, e0f, 0.0)
-    ri, rd = R.merge_branches(ids_r[..., :10].contiguous(), dist_r[..., :10].contiguous(), 10)
-    theirs = _recall(ri.cpu().numpy(), truth, 10)
+    theirs = _recall(ref[0].cpu().numpy(), truth, 10)
     assert abs(mine - theirs) <= 0.005, (mine, theirs)
+
+
+@pytest.mark.parametrize("stall,crowd,V,policy", [
+    (1, 0.0, 1, 0), (3, 0.0, 1, 0), (2, 0.0, 4, 1),
+    (0, 0.3, 1, 0), (0, 0.4, 1, 0), (0, 0.3, 4, 0), (0, 0.5, 4, 1), (2, 0.4, 3, 1),
+])
+def test_stall_and_crowd_rules_bitwise(stall, crowd, V, policy):
+    """The stall rule (stop once the k-th best has not improved for `stall`
+    steps) and the crowd rule (retire a lineage after two expansions whose
+    neighbours were mostly covered already) of local_search.cu:659-682: queues,
+    distances, flags, lineage and every counter -- stalled and crowded included
+    -- equal the oracle and the reference's own kernels bit for bit, through
+    advance and through the fused kernel."""
+    X, G = cases.toy(seed=211)
+    rng = np.random.default_rng(stall * 10 + V)
+    nq, J, L, B = 8, 3, 16, 40
+    Qv = cases.unit_queries(nq, X.shape[1], 5 + V)
+    seeds = rng.integers(0, X.shape[0], (nq, J, V)).astype(np.int32)
+    Xg, Gg, Qg = to_gpu(X, G, Qv)
+    kw = dict(L=L, B=B, D=G.shape[1], team_size=16, policy=policy, stop_eps=-1.0, kstop=10,
+              stall_patience=stall, crowd_frac=crowd)
+    st = E.init_states(Xg, Qg, torch.from_numpy(seeds), **kw)
+    E.advance(Xg, Gg, Qg, st, B)
+    st.check()
+    if stall:
+        assert int(st.stalled.sum()) > 0, "the stall rule never fired: the case tests nothing"
+    if crowd:
+        assert int(st.crowded.sum()) > 0, "the crowd rule never fired: the case tests nothing"
+    gi, gd = st.ids.cpu().numpy(), st.dist.cpu().numpy()
+    ge, gl, gc = st.expanded.cpu().numpy(), st.lineage.cpu().numpy(), st.counters.cpu().numpy()
+    for q in range(nq):
+        for j in range(J):
+            r = O.branch_run(X, G, Qv[q], seeds[q, j], L=L, B=B, team=16, policy=policy, stall_patience=stall,
+                             crowd_frac=crowd)
+            tag = f"q={q} j={j}"
+            assert np.array_equal(r["ids"], gi[q, j]), tag
+            assert np.array_equal(r["dist"].view(np.int32), gd[q, j].view(np.int32)), tag
+            assert np.array_equal(r["expanded"], ge[q, j]), tag
+            assert np.array_equal(r["lineage"], gl[q, j]), tag
+            for c in (0, 1, 3, 6, 7, 8, 9):
+                assert r["counters"][c] == gc[q, j, c], f"{tag} counter {c}"
+    ref = ref_run(Xg, Gg, Qg, torch.from_numpy(seeds), L, B, 0, 16, policy=policy, stall=stall, crowd=crowd)
+    if ref is not None:
+        same_state(st, ref, counters=(0, 1, 2, 3, 6, 7, 8, 9))
+    # the fused kernel runs the same walk in one launch
+    fi, fd, fst = E.search(Xg, Gg, Qg, torch.from_numpy(seeds), k=10, L=L, B=B, team_size=16, policy=policy,
+                           stall_patience=stall, crowd_frac=crowd)
+    assert torch.equal(fst.ids, st.ids) and torch.equal(fst.counters, st.counters)
