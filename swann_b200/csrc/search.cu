@@ -912,18 +912,30 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
     for (int t = w + lane; t < k; t += 32) { oi[t] = -1; od[t] = __int_as_float(0x7f800000); }
 }
 
-// Register budget of the fused kernel: 65536 / (256 * 6) -> 40 registers a
+// Register budget of the fused kernel: 65536 / (128 * 12) -> 40 registers a
 // thread, 12 CTAs of 4 warps (4 branches) an SM.  Measured at C3 (1M x 1536
 // fp16, batch 65535): occupancy buys more than the spills it costs.  With the
 // whole-row L2 prefetch and one row a team, 40 registers and 3-chunk segments
 // ran 767k QPS, 48 registers and 4-chunk segments 744-748k, 40 registers and
 // 4-chunk segments 732k, 32 registers 710k; 80 registers (no spills) ran
 // slowest of all.  Two rows a team: 40 registers 819-856k, 48 registers 852k.
+// Kernel-only at C3 (65535 queries, two rows a team, 40 registers: 68.8-70.5
+// ms), measured against: three rows at 48 / 64 registers 77.4 / 73.8 ms, four
+// rows at 64 registers 74.9 ms, 2-chunk segments at 56 registers 73.9 ms; an
+// L1 line prefetch of the next segment (loads allocating in L1) 77.6 ms; each
+// lane's chunks staged through a cp.async ring in shared memory (2-8 in
+// flight, 9-6 CTAs an SM) 117-133 ms.
+// Threads of a fused-search CTA (4 warps: 4 branches of one query) and the
+// CTAs an SM should hold; 12 CTAs of 128 threads give ptxas 40 registers a
+// thread.
+#ifndef SWB_FUSED_THREADS
+#define SWB_FUSED_THREADS 128
+#endif
 #ifndef SWB_FUSED_MINB
-#define SWB_FUSED_MINB 6
+#define SWB_FUSED_MINB 12
 #endif
 template <int TEAM, typename XT, int NT>
-__global__ void __launch_bounds__(256, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
+__global__ void __launch_bounds__(SWB_FUSED_THREADS, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.y;
@@ -1241,10 +1253,10 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.status = status; K.k = k; K.kk = k < L ? k : L;
     K.branch_ids = branch_ids; K.branch_dist = branch_dist; K.qdone = qdone;
     K.out_ids = out_ids; K.out_dist = out_dist;
-    int W = abi::env_int("SWB_WARPS", 4);
+    int W = abi::env_int("SWB_WARPS", SWB_FUSED_THREADS / 32);
     if (W > J) W = J;
     if (W < 1) W = 1;
-    if (W > 8) W = 8;
+    if (W > SWB_FUSED_THREADS / 32) W = SWB_FUSED_THREADS / 32;
     K.W = W;
     dim3 grid((unsigned)((J + W - 1) / W), (unsigned)Q);
     const size_t smem = (size_t)query_bytes(dim) + (size_t)W * K.warp_bytes;

@@ -104,8 +104,8 @@ def test_shared_table_round_trips_through_the_reference_layout(fp16):
     """A per-query table shared by 6 branches, no claims and no bound (so the
     walk is deterministic): queues bit for bit, the table holds the same
     (node, distance) entries as the reference kernels' cache_id / cache_d --
-    also when carried between advance calls -- and each query's total of
-    claims and hits matches."""
+    also when carried between advance calls -- and each branch's evaluations
+    plus table hits match."""
     R = _ref()
     X, G = cases.toy(seed=77)
     Xs = X.astype(np.float16) if fp16 else X
@@ -120,10 +120,13 @@ def test_shared_table_round_trips_through_the_reference_layout(fp16):
     for key in ("ids", "expd", "lin"):
         assert torch.equal(mine[key], theirs[key]), key
     assert torch.equal(mine["dist"].view(torch.int32), theirs["dist"].view(torch.int32))
-    for c in (0, 1, 3, 8, 9):
+    for c in (0, 3, 8, 9):
         assert torch.equal(mine["ctr"][..., c], theirs["ctr"][..., c]), c
-    for c in (4, 5):
-        assert torch.equal(mine["ctr"][..., c].sum(1), theirs["ctr"][..., c].sum(1)), c
+    # which branch scores a node first is a race in both implementations, so
+    # evaluations and hits split differently between branches; every fresh
+    # neighbour is one or the other, so their sum per branch is fixed
+    both = lambda st: st["ctr"][..., 1] + st["ctr"][..., 4]  # noqa: E731
+    assert torch.equal(both(mine), both(theirs))
     assert _entries(mine["cid"], mine["cdd"]) == _entries(theirs["cid"], theirs["cdd"])
     # every slot the reference leaves empty reads (0, FLT_MAX) here too
     empty = mine["cid"] == 0

@@ -136,7 +136,7 @@ def test_c3_shaped_recall_matches_reference_kernel():
     rel = np.abs(dist.astype(np.float64) - ex) / np.maximum(np.abs(ex), 1e-30)
     assert ok.all() and rel.max() <= 1e-5, rel.max()
     assert mine >= 0.9, mine
-    ent = S.select_nearest(Qg, S.pool_vectors(Xg, cat), 32, metric=0)
+    ent = S.select_nearest(Qg, S.pool_vectors(Xg, cat).float(), 32, metric=0)
     ref = ref_production(Xg, G, Qg, cat[ent].to(torch.int32), k=10, L=12, B=64, metric=0, team=16, stop_eps=0.01)
     if ref is None:
         pytest.skip("reference kernels not built")
