@@ -272,48 +272,58 @@ def build_index(cfg, dev, world, rank):
         torch.cuda.synchronize()
         t["generate_s"] = time.perf_counter() - t0
         t1 = time.perf_counter()
-        cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"])
+        ops = B.TcOperands(X)       # the rows as the tensor cores read them, shared by the three stages
+        cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"], ops=ops)
         torch.cuda.synchronize()
         t["sweep_s"] = time.perf_counter() - t1
         t1 = time.perf_counter()
-        G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"])
+        G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"], ops=ops)
         torch.cuda.synchronize()
         t["prune_s"] = time.perf_counter() - t1
         del cand, cd
         t1 = time.perf_counter()
-        G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"])
+        G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"], ops=ops)
         torch.cuda.synchronize()
         t["reverse_s"] = time.perf_counter() - t1
+        t["exact_recomputed_pairs"] = int(ops.recomputed[0])
+        del ops
     else:
         a, b = D.shard_bounds(n, world)[rank]
         Xl = make_corpus(cfg, dev, rows=(a, b))   # this rank's row block is its input
         torch.cuda.synchronize()
         t["generate_s"] = time.perf_counter() - t0
         stage = {}
+        shared = {}
+
+        def operands(Xa):
+            if "ops" not in shared:
+                shared["ops"] = B.TcOperands(Xa)
+            return shared["ops"]
 
         def sweep(Xa, r0, r1):
             s = time.perf_counter()
-            c, d = B.knn_candidates(Xa, 128, metric=cfg["metric"], rows=(r0, r1))
+            c, d = B.knn_candidates(Xa, 128, metric=cfg["metric"], rows=(r0, r1), ops=operands(Xa))
             torch.cuda.synchronize()
             stage["sweep_s"] = time.perf_counter() - s
             return c, d
 
         def prune(Xa, c, d):
             s = time.perf_counter()
-            g = B.robust_prune(Xa, c, d, 64, alpha=1.2, metric=cfg["metric"])
+            g = B.robust_prune(Xa, c, d, 64, alpha=1.2, metric=cfg["metric"], ops=operands(Xa))
             torch.cuda.synchronize()
             stage["prune_s"] = time.perf_counter() - s
             return g
 
         def reverse(Xa, G1, r0, r1):
             s = time.perf_counter()
-            g = B.add_reverse(Xa, G1, 64, alpha=1.2, metric=cfg["metric"], rows=(r0, r1))
+            g = B.add_reverse(Xa, G1, 64, alpha=1.2, metric=cfg["metric"], rows=(r0, r1), ops=operands(Xa))
             torch.cuda.synchronize()
             stage["reverse_s"] = time.perf_counter() - s
             return g
 
         X, G = D.build_sharded(Xl, n, sweep, prune, reverse)
         t.update(stage)
+        shared.clear()
     torch.cuda.synchronize()
     t["total_s"] = time.perf_counter() - t0
     return X, G, t
@@ -812,15 +822,18 @@ def run_build(args):
     n, d = X.shape
     with ClockSampler(local) as clk:
         t0 = time.perf_counter()
-        cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"])
+        ops = B.TcOperands(X)
+        cand, cd = B.knn_candidates(X, 128, metric=cfg["metric"], ops=ops)
         torch.cuda.synchronize()
         t1 = time.perf_counter()
-    G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"])
+    G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"], ops=ops)
     torch.cuda.synchronize()
     t2 = time.perf_counter()
-    G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"])
+    G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"], ops=ops)
     torch.cuda.synchronize()
     t3 = time.perf_counter()
+    recomputed = int(ops.recomputed[0])
+    del ops
     roof = sweep_roofline({"sweep_s": t1 - t0}, n, d, cfg["half"])
     if peaks_fp32:
         roof["measured_fp32_gemm"] = peaks_fp32
@@ -834,6 +847,7 @@ def run_build(args):
             "stages_s": {"sweep": round(t1 - t0, 3), "prune": round(t2 - t1, 3), "reverse": round(t3 - t2, 3)},
             "roofline": roof,
             "prune_tflops": round(prune_flops / (t2 - t1) / 1e12, 1),
+            "prune": os.environ.get("SWB_PRUNE", "tc"), "exact_recomputed_pairs": recomputed,
             "clocks_during_sweep": clk.summary(),
             "mean_out_degree": round(float((G >= 0).sum(1).float().mean()), 2)}
     if not args.no_cpu:

@@ -239,6 +239,28 @@ SWB_API int swb_prune(const float* X, int64_t n, int dim, const int32_t* cand, c
               int64_t rows, int C, int deg, float alpha, int metric,
               const int32_t* deg_per_node, const uint8_t* protect, int32_t* out, void* stream);
 
+/* Replaces robust_prune (swann/build.py:48-91) as swb_prune does, with the
+ * pair distances on the tensor cores and the same output, bit for bit: each
+ * node's 128 x 128 candidate Gram matrix is formed with tcgen05 (kind::f16
+ * for fp16-valued rows, 3xTF32 otherwise), every detour test that clears its
+ * threshold by more than a rigorous bound on the tensor-core value's gap to
+ * the dimension-ordered fmaf chain is decided from it, and the pairs within
+ * the bound are recomputed with that fmaf chain.
+ *   A        tensor-core operand rows [n, adim]: a_dtype SWB_F16 -> the rows in
+ *            fp16 (they must be fp16-valued), SWB_F32 -> their tf32 high parts
+ *            with A_lo the low parts (swb_split_tf32); zero-padded to adim, a
+ *            multiple of 64 (f16) or 32 (f32); 16-byte aligned
+ *   X        the fp32 rows [n, dim] (the exact recompute)
+ *   norms    [n] squared norms of X by swb_row_norms (both metrics)
+ *   recomputed optional device uint64: += the pairs recomputed exactly
+ *   status   optional int32 device word: SWB_ERR_TIMEOUT if a wait ran out
+ *   other arguments as swb_prune */
+SWB_API int swb_prune_tc(const float* X, const void* A, const void* A_lo, int a_dtype, int adim,
+                 const float* norms, int64_t n, int dim, const int32_t* cand, const float* cdist,
+                 int64_t rows, int C, int deg, float alpha, int metric, const int32_t* deg_per_node,
+                 const uint8_t* protect, int32_t* out, unsigned long long* recomputed, int32_t* status,
+                 void* stream);
+
 /* Replaces add_reverse (swann/build.py:96-150): offers every edge of G back to
  * its target (first `max_in` offers per target in source order), merges with
  * the target's own row, drops self and duplicates, scores, keeps the nearest
@@ -252,6 +274,13 @@ SWB_API int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G, in
                 int max_in, int metric, const int32_t* deg_per_node, int64_t row0, int64_t rows,
                 int32_t* out, void* workspace, uint64_t ws_bytes, void* stream);
 SWB_API uint64_t swb_reverse_workspace(int64_t n, int64_t rows, int deg, int max_in);
+/* swb_reverse with its re-prune on the tensor cores (swb_prune_tc's operands
+ * and guarantee: the same output as swb_reverse, bit for bit). */
+SWB_API int swb_reverse_tc(const float* X, const void* A, const void* A_lo, int a_dtype, int adim,
+                   const float* norms, int64_t n, int dim, const int32_t* G, int deg, float alpha,
+                   int max_in, int metric, const int32_t* deg_per_node, int64_t row0, int64_t rows,
+                   int32_t* out, void* workspace, uint64_t ws_bytes, unsigned long long* recomputed,
+                   int32_t* status, void* stream);
 
 /* ------------------------------------------------- offline builder extras -- */
 

@@ -16,7 +16,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libswann_b200.so"
-SOURCES = ["search.cu", "build.cu", "sweep_mma.cu", "select.cu", "offline.cu"]
+SOURCES = ["search.cu", "build.cu", "sweep_mma.cu", "prune_tc.cu", "select.cu", "offline.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # The search's distance sums must round every multiply and add on its own (the
 # reference builds with -fmad=false too); ptxas would otherwise fuse the packed

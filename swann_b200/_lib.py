@@ -55,6 +55,10 @@ SIGNATURES = {
     "swb_prune": (_i32, [_vp, _i64, _i32, _vp, _vp, _i64, _i32, _i32, _f32, _i32, _vp, _vp, _vp, _vp]),
     "swb_reverse": (_i32, [_vp, _i64, _i32, _vp, _i32, _f32, _i32, _i32, _vp, _i64, _i64, _vp, _vp, _u64, _vp]),
     "swb_reverse_workspace": (_u64, [_i64, _i64, _i32, _i32]),
+    "swb_prune_tc": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp, _i64, _i32, _vp, _vp, _i64, _i32, _i32, _f32, _i32,
+                            _vp, _vp, _vp, _vp, _vp, _vp]),
+    "swb_reverse_tc": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp, _i64, _i32, _vp, _i32, _f32, _i32, _i32, _vp, _i64,
+                              _i64, _vp, _vp, _u64, _vp, _vp, _vp]),
     "swb_last_error": (C.c_char_p, []),
     "swb_version": (_i32, []),
 }

@@ -7,13 +7,16 @@ Drop-in for swann/build.py (geniussyn/SWANN): `pairwise`, `knn_candidates`,
                   is scored against the whole corpus and each row's C nearest
                   are selected by swb_topc_block (native); the dot products of
                   the chunk come from a tensor-core GEMM.
-  robust_prune    swb_prune: one block per node, the candidates' Gram matrix
-                  in shared memory, the reference's sequential keep rule.
-  add_reverse     swb_reverse: stable radix sort of the edges by target, row
+  robust_prune    swb_prune_tc: one block per node, the candidates' Gram
+                  matrix on the tensor cores, the reference's sequential keep
+                  rule (swb_prune: the same on CUDA cores).
+  add_reverse     swb_reverse_tc: stable radix sort of the edges by target, row
                   merge + scoring, then the same prune.
 
-The prune and reverse passes accumulate every dot product in dimension order
-with fmaf, so their output is reproducible bit for bit from the same input.
+The prune and reverse passes decide every detour test as a dimension-ordered
+fmaf dot product would (the tensor-core pass recomputes with that chain every
+pair its own values cannot decide for certain), so their output is
+reproducible bit for bit from the same input.
 """
 from __future__ import annotations
 
@@ -70,6 +73,47 @@ def _dots(A, B, exact_half):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+class TcOperands:
+    """A corpus's rows as the tensor cores read them, prepared once and shared
+    by the sweep, the prune and the reverse pass: fp16 rows (fp16-valued
+    corpora, padded to a multiple of 64 columns) or tf32 high and low parts
+    (padded to a multiple of 32), the fp32 rows, and their squared norms in
+    the fmaf-chain order the prune's pair distances use."""
+
+    def __init__(self, Xg, half_exact=None):
+        Xg = Xg.contiguous()
+        if half_exact is None:
+            small = Xg.shape[0] * Xg.shape[1] <= (1 << 26)
+            half_exact = bool(Xg.dtype == torch.float16 or (small and torch.equal(Xg.float(), Xg.half().float())))
+        self.half = half_exact
+        self.X = Xg.float().contiguous()
+        self.norms = row_norms(self.X)
+        self.dim = self.X.shape[1]
+        if half_exact:
+            self.A, self.A_lo, self.code = _pad_cols(Xg.half().contiguous(), 64), None, N.F16
+        else:
+            Xp = _pad_cols(self.X, 32)
+            self.A, self.A_lo = torch.empty_like(Xp), torch.empty_like(Xp)
+            with torch.cuda.device(Xg.device):
+                N.check(N.lib().swb_split_tf32(N.ptr(Xp), Xp.numel(), N.ptr(self.A), N.ptr(self.A_lo),
+                                               N.stream_of(Xg)), "split")
+            self.code = N.F32
+        self.adim = self.A.shape[1]
+        self.recomputed = torch.zeros(1, dtype=torch.int64, device=Xg.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=Xg.device)
+
+    def check(self):
+        if int(self.status[0]) != 0:
+            raise N.SwannError(int(self.status[0]), "a device-side wait timed out in the tensor-core prune")
+
+
+def _prune_method(method):
+    method = method or os.environ.get("SWB_PRUNE", "tc")
+    if method not in ("tc", "simt"):
+        raise ValueError("prune method must be 'tc' or 'simt'")
+    return method
+
+
 def _pad_cols(X, mult):
     d = X.shape[1]
     if d % mult == 0:
@@ -81,7 +125,7 @@ def _pad_cols(X, mult):
 
 @torch.no_grad()
 def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact=None, rows=None,
-                   method=None, row_block=1 << 18):
+                   method=None, row_block=1 << 18, ops=None):
     """Exact top-C neighbours by the corpus's metric, self excluded
     (swann/build.py:30-43).  Returns (idx int32 [m, C], dst f32 [m, C]) for
     rows=(r0, r1) (default: every row), m = r1 - r0.
@@ -93,7 +137,7 @@ def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact
     if method is None:
         method = os.environ.get("SWB_SWEEP", "mma")
     if method == "mma":
-        return _knn_mma(Xg, C, metric, half_exact, rows, row_block)
+        return _knn_mma(Xg, C, metric, half_exact, rows, row_block, ops)
     m = _m(metric)
     if not Xg.is_cuda:
         raise ValueError("vectors must be on the GPU")
@@ -122,23 +166,15 @@ def knn_candidates(Xg, C, chunk=4096, metric="ip", col_chunk=1 << 20, half_exact
     return idx, dst
 
 
-def _knn_mma(Xg, C, metric, half_exact, rows, row_block):
+def _knn_mma(Xg, C, metric, half_exact, rows, row_block, ops=None):
     m = _m(metric)
     if not Xg.is_cuda:
         raise ValueError("vectors must be on the GPU")
     n = Xg.shape[0]
-    if half_exact is None:
-        small = n * Xg.shape[1] <= (1 << 26)
-        half_exact = bool(Xg.dtype == torch.float16 or (small and torch.equal(Xg.float(), Xg.half().float())))
-    norms = row_norms(Xg.float().contiguous()) if m == METRIC_L2 else None
-    if half_exact:
-        lo = None
-        hi = _pad_cols(Xg.half().contiguous(), 64)
-        code = N.F16
-    else:
-        Xf = _pad_cols(Xg.float().contiguous(), 32)
-        hi = torch.empty_like(Xf)
-        lo = torch.empty_like(Xf)
+    if ops is None:
+        ops = TcOperands(Xg, half_exact)
+    norms = ops.norms if m == METRIC_L2 else None
+    hi, lo, code = ops.A, ops.A_lo, ops.code
     R0, R1 = (0, n) if rows is None else rows
     idx = torch.empty((R1 - R0, C), dtype=torch.int32, device=Xg.device)
     dst = torch.empty((R1 - R0, C), dtype=torch.float32, device=Xg.device)
@@ -146,10 +182,6 @@ def _knn_mma(Xg, C, metric, half_exact, rows, row_block):
     lib = N.lib()
     with torch.cuda.device(Xg.device):
         s = N.stream_of(Xg)
-        if not half_exact:
-            N.check(lib.swb_split_tf32(N.ptr(Xf), Xf.numel(), N.ptr(hi), N.ptr(lo), s), "split")
-            del Xf
-            code = N.F32
         for r0 in range(R0, R1, row_block):
             r1 = min(R1, r0 + row_block)
             ws_bytes = int(lib.swb_sweep_workspace(n, r1 - r0, C, code))
@@ -167,13 +199,17 @@ def _knn_mma(Xg, C, metric, half_exact, rows, row_block):
 
 
 @torch.no_grad()
-def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None, metric="ip", protect=None):
+def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None, metric="ip", protect=None,
+                 method=None, ops=None):
     """Keep a candidate only when no nearer kept neighbour detours to it
     (swann/build.py:48-91).  Returns int32 [n, width], -1 padded: width = deg,
     or the largest of `deg_per_node` (per-node caps, int [n]) when given.
     `protect` (bool [n, C], e.g. mutual_rank's) exempts a candidate from the
-    detour test."""
-    Xf = Xg.float().contiguous()
+    detour test.  method "tc" (default; SWB_PRUNE overrides): pair distances
+    on the tensor cores, `ops` (TcOperands) prepared once per corpus; "simt":
+    on CUDA cores.  Both give the same graph, bit for bit."""
+    method = _prune_method(method)
+    Xf = ops.X if (method == "tc" and ops is not None) else Xg.float().contiguous()
     cand = cand.to(torch.int32).contiguous()
     cdist = cdist.float().contiguous()
     n, C = cand.shape
@@ -191,20 +227,33 @@ def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None,
             raise ValueError("protect must have the candidate matrix's shape")
     out = torch.empty((n, width), dtype=torch.int32, device=Xg.device)
     with torch.cuda.device(Xg.device):
-        rc = N.lib().swb_prune(N.ptr(Xf), Xf.shape[0], Xf.shape[1], N.ptr(cand), N.ptr(cdist), n, C, width,
-                               float(alpha), _m(metric), N.ptr(dpn), N.ptr(prot), N.ptr(out), N.stream_of(Xg))
+        if method == "tc":
+            ops = ops or TcOperands(Xg)
+            rc = N.lib().swb_prune_tc(N.ptr(ops.X), N.ptr(ops.A), N.ptr(ops.A_lo), ops.code, ops.adim,
+                                      N.ptr(ops.norms), Xf.shape[0], Xf.shape[1], N.ptr(cand), N.ptr(cdist), n, C,
+                                      width, float(alpha), _m(metric), N.ptr(dpn), N.ptr(prot), N.ptr(out),
+                                      N.ptr(ops.recomputed), N.ptr(ops.status), N.stream_of(Xg))
+        else:
+            rc = N.lib().swb_prune(N.ptr(Xf), Xf.shape[0], Xf.shape[1], N.ptr(cand), N.ptr(cdist), n, C, width,
+                                   float(alpha), _m(metric), N.ptr(dpn), N.ptr(prot), N.ptr(out), N.stream_of(Xg))
     N.check(rc, "robust_prune")
+    if method == "tc":
+        ops.check()
     return out
 
 
 @torch.no_grad()
-def add_reverse(Xg, G, deg, chunk=2048, alpha=1.2, max_in=64, deg_per_node=None, metric="ip", rows=None):
+def add_reverse(Xg, G, deg, chunk=2048, alpha=1.2, max_in=64, deg_per_node=None, metric="ip", rows=None,
+                method=None, ops=None):
     """Offer every edge back to its target, then re-prune the union per node
     (swann/build.py:96-150).  rows=(r0, r1) re-prunes only those rows (a
     rank's block of a sharded build); G is always the whole graph.  With
     `deg_per_node` (int [n]) the caps are per node and the width is their
-    largest, as robust_prune writes it."""
-    Xf = Xg.float().contiguous()
+    largest, as robust_prune writes it.  `method` / `ops` as robust_prune."""
+    method = _prune_method(method)
+    if method == "tc":
+        ops = ops or TcOperands(Xg)
+    Xf = ops.X if method == "tc" else Xg.float().contiguous()
     G = G.to(torch.int32).contiguous()
     n = G.shape[0]
     r0, r1 = (0, n) if rows is None else rows
@@ -221,9 +270,18 @@ def add_reverse(Xg, G, deg, chunk=2048, alpha=1.2, max_in=64, deg_per_node=None,
     ws_bytes = int(lib.swb_reverse_workspace(n, r1 - r0, G.shape[1], max_in))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=Xg.device)
     with torch.cuda.device(Xg.device):
-        rc = lib.swb_reverse(N.ptr(Xf), n, Xf.shape[1], N.ptr(G), int(deg), float(alpha), int(max_in), _m(metric),
-                             N.ptr(dpn), r0, r1 - r0, N.ptr(out), N.ptr(ws), ws_bytes, N.stream_of(Xg))
+        if method == "tc":
+            rc = lib.swb_reverse_tc(N.ptr(Xf), N.ptr(ops.A), N.ptr(ops.A_lo), ops.code, ops.adim, N.ptr(ops.norms),
+                                    n, Xf.shape[1], N.ptr(G), int(deg), float(alpha), int(max_in), _m(metric),
+                                    N.ptr(dpn), r0, r1 - r0, N.ptr(out), N.ptr(ws), ws_bytes,
+                                    N.ptr(ops.recomputed), N.ptr(ops.status), N.stream_of(Xg))
+        else:
+            rc = lib.swb_reverse(N.ptr(Xf), n, Xf.shape[1], N.ptr(G), int(deg), float(alpha), int(max_in),
+                                 _m(metric), N.ptr(dpn), r0, r1 - r0, N.ptr(out), N.ptr(ws), ws_bytes,
+                                 N.stream_of(Xg))
     N.check(rc, "add_reverse")
+    if method == "tc":
+        ops.check()
     return out
 
 
@@ -233,7 +291,9 @@ def build_graph(X, metric: str = "ip", degree: int = 96, candidates: int = 128, 
     if X.device.type != "cuda":
         X = X.cuda()
     Xg = X.contiguous()
-    cand, cdist = knn_candidates(Xg, candidates, metric=metric)
-    G = robust_prune(Xg, cand, cdist, degree, alpha=alpha, metric=metric)
-    G = add_reverse(Xg, G, degree, alpha=alpha, metric=metric)
+    ops = TcOperands(Xg)
+    cand, cdist = knn_candidates(Xg, candidates, metric=metric, ops=ops)
+    G = robust_prune(Xg, cand, cdist, degree, alpha=alpha, metric=metric, ops=ops)
+    del cand, cdist
+    G = add_reverse(Xg, G, degree, alpha=alpha, metric=metric, ops=ops)
     return G.to(torch.int32).contiguous()

@@ -602,9 +602,54 @@ extern "C" uint64_t swb_reverse_workspace(int64_t n, int64_t rows, int deg, int 
     return b;
 }
 
+// The tensor-core prune (prune_tc.cu).
+int swb_prune_tc_launch(const float* X, const void* A, const void* A_lo, int a_dtype, int adim, const float* norms,
+                        int64_t n, int dim, const int32_t* cand, const float* cdist, int64_t rows, int C, int deg,
+                        float alpha, int metric, const int32_t* deg_per_node, const uint8_t* protect, int32_t* out,
+                        unsigned long long* recomputed, int32_t* status, cudaStream_t st);
+
+namespace {
+
+// The operands of a tensor-core prune (A == nullptr: the CUDA-core prune).
+struct TcOps {
+    const void* A;
+    const void* A_lo;
+    int a_dtype, adim;
+    const float* norms;
+    unsigned long long* recomputed;
+    int32_t* status;
+};
+
+int reverse_impl(const float* X, int64_t n, int dim, const int32_t* G, int deg, float alpha, int max_in, int metric,
+                 const int32_t* deg_per_node, int64_t row0, int64_t rows, int32_t* out, void* workspace,
+                 uint64_t ws_bytes, const TcOps& tc, cudaStream_t st);
+
+}  // namespace
+
 extern "C" int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G, int deg, float alpha, int max_in,
                            int metric, const int32_t* deg_per_node, int64_t row0, int64_t rows, int32_t* out,
                            void* workspace, uint64_t ws_bytes, void* stream) {
+    const TcOps none{nullptr, nullptr, 0, 0, nullptr, nullptr, nullptr};
+    return reverse_impl(X, n, dim, G, deg, alpha, max_in, metric, deg_per_node, row0, rows, out, workspace, ws_bytes,
+                        none, (cudaStream_t)stream);
+}
+
+extern "C" int swb_reverse_tc(const float* X, const void* A, const void* A_lo, int a_dtype, int adim,
+                              const float* norms, int64_t n, int dim, const int32_t* G, int deg, float alpha,
+                              int max_in, int metric, const int32_t* deg_per_node, int64_t row0, int64_t rows,
+                              int32_t* out, void* workspace, uint64_t ws_bytes, unsigned long long* recomputed,
+                              int32_t* status, void* stream) {
+    if (!A || !norms) return abi::fail(SWB_ERR_ARG, "the tensor-core reverse pass needs its operand rows and norms");
+    const TcOps tc{A, A_lo, a_dtype, adim, norms, recomputed, status};
+    return reverse_impl(X, n, dim, G, deg, alpha, max_in, metric, deg_per_node, row0, rows, out, workspace, ws_bytes,
+                        tc, (cudaStream_t)stream);
+}
+
+namespace {
+
+int reverse_impl(const float* X, int64_t n, int dim, const int32_t* G, int deg, float alpha, int max_in, int metric,
+                 const int32_t* deg_per_node, int64_t row0, int64_t rows, int32_t* out, void* workspace,
+                 uint64_t ws_bytes, const TcOps& tc, cudaStream_t st) {
     if (!X || !G || !out || !workspace) return abi::fail(SWB_ERR_ARG, "null buffer");
     if (n <= 0 || rows <= 0) return SWB_OK;
     if (row0 < 0 || row0 + rows > n) return abi::fail(SWB_ERR_ARG, "row range outside the graph");
@@ -612,7 +657,6 @@ extern "C" int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G,
     if (total >= (int64_t)1 << 31) return abi::fail(SWB_ERR_ARG, "n * degree must be below 2^31");
     if (ws_bytes < swb_reverse_workspace(n, rows, deg, max_in)) return abi::fail(SWB_ERR_ARG, "workspace too small");
     if (deg + max_in > 256) return abi::fail(SWB_ERR_ARG, "degree + max_in must be at most 256");
-    cudaStream_t st = (cudaStream_t)stream;
     const int keepn = (deg + max_in) < 128 ? (deg + max_in) : 128;
     char* p = (char*)workspace;
     int32_t* keys = (int32_t*)p; p += align256(total * 4);
@@ -645,9 +689,14 @@ extern "C" int swb_reverse(const float* X, int64_t n, int dim, const int32_t* G,
                                                                n, row0, cand, cdist);
     rc = abi::cuda_check("reverse merge launch");
     if (rc) return rc;
-    return launch_prune(X, n, rows, dim, cand, cdist, keepn, deg, alpha, metric,
-                        deg_per_node ? deg_per_node + row0 : nullptr, nullptr, out, st);
+    const int32_t* dpn = deg_per_node ? deg_per_node + row0 : nullptr;
+    if (tc.A)
+        return swb_prune_tc_launch(X, tc.A, tc.A_lo, tc.a_dtype, tc.adim, tc.norms, n, dim, cand, cdist, rows, keepn,
+                                   deg, alpha, metric, dpn, nullptr, out, tc.recomputed, tc.status, st);
+    return launch_prune(X, n, rows, dim, cand, cdist, keepn, deg, alpha, metric, dpn, nullptr, out, st);
 }
+
+}  // namespace
 
 extern "C" const char* swb_last_error(void) { return abi::last_error().c_str(); }
 extern "C" int swb_version(void) { return 1; }

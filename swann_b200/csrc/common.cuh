@@ -235,6 +235,19 @@ __device__ __forceinline__ uint4 ld_row16(const uint4* p) {
     return v;
 }
 
+// Asynchronous 16-byte global -> shared copy (cp.async, cached in L2 only):
+// the bytes travel without occupying a register; the issuing thread waits for
+// them with cp_async_wait.  Both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's committed groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // A whole row into L2 with one instruction (16-byte aligned, size a multiple
 // of 16): issued as a team starts a row, it turns the row's later segments
 // into L2 hits instead of dependent DRAM round trips.

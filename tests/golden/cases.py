@@ -126,3 +126,13 @@ def aniso_mixture(n, d, clusters, seed, nq=0, qseed=None):
     X = draw(n, np.random.default_rng(seed + 1))
     Q = draw(nq, np.random.default_rng(seed + 2 if qseed is None else qseed)) if nq else None
     return X, Q
+
+
+def iso_mixture(n, d, clusters, seed, sigma=0.3):
+    """BASELINE config 5's corpus model (and config 2's): `clusters` centres
+    N(0, 1)^d, isotropic sigma, float32, not normalised (an L2 corpus)."""
+    g = np.random.default_rng(seed)
+    centres = g.standard_normal((clusters, d), dtype=np.float32)
+    c = g.integers(0, clusters, n)
+    X = centres[c] + sigma * g.standard_normal((n, d), dtype=np.float32)
+    return np.ascontiguousarray(X, dtype=np.float32)

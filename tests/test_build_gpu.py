@@ -136,3 +136,64 @@ def test_build_graph_end_to_end(metric):
     G1 = O.robust_prune(X, c, d, 32, 1.2, metric)
     G2 = O.add_reverse(X, G1, 32, 1.2, 64, metric)
     assert np.array_equal(G, G2)
+
+
+def _prune_case(kind):
+    """Production widths: C3's model (d = 1536, fp16-valued unit rows, ip) and
+    C5's (d = 1024 fp32 mixture rows, l2), 4000 rows, 128 candidates each
+    from the GPU sweep."""
+    if kind == "c3":
+        X, _ = cases.aniso_mixture(4000, 1536, clusters=40, seed=3)
+        X = X.astype(np.float16).astype(np.float32)
+        return X, "ip", torch.from_numpy(X.astype(np.float16)).to(DEV)
+    X = cases.iso_mixture(4000, 1024, clusters=40, seed=4)
+    return X, "l2", torch.from_numpy(X).to(DEV)
+
+
+@pytest.mark.parametrize("kind", ["c3", "c5"])
+def test_tensor_core_prune_equals_fmaf_prune_at_production_widths(kind, monkeypatch):
+    """The tensor-core prune (kind::f16 for C3's fp16 rows, 3xTF32 for C5's
+    fp32 rows) returns the CUDA-core prune's graph and the oracle's, bit for
+    bit, given the same candidates -- with its near-threshold pairs decided by
+    the exact recompute (some are, at these sizes), and also when every pair
+    is sent there (the bound forced to infinity)."""
+    X, name, Xg = _prune_case(kind)
+    metric = 0 if name == "ip" else 1
+    cand, cd = B.knn_candidates(Xg, 128, metric=name)
+    ops = B.TcOperands(Xg)
+    tc = B.robust_prune(Xg, cand, cd, 64, alpha=1.2, metric=name, method="tc", ops=ops)
+    assert int(ops.recomputed[0]) > 0, "no pair reached the exact recompute: the case tests only half the path"
+    simt = B.robust_prune(Xg, cand, cd, 64, alpha=1.2, metric=name, method="simt")
+    assert torch.equal(tc, simt)
+    want = O.robust_prune(X, cand.cpu().numpy(), cd.cpu().numpy(), 64, 1.2, metric, threads=O.cpu_count())
+    assert np.array_equal(tc.cpu().numpy(), want)
+    monkeypatch.setenv("SWB_PRUNE_TOL_SCALE", "inf")
+    forced = B.robust_prune(Xg, cand, cd, 64, alpha=1.2, metric=name, method="tc", ops=B.TcOperands(Xg))
+    assert torch.equal(forced, tc)
+
+
+@pytest.mark.parametrize("kind", ["c3", "c5"])
+def test_tensor_core_reverse_equals_fmaf_reverse_at_production_widths(kind):
+    X, name, Xg = _prune_case(kind)
+    cand, cd = B.knn_candidates(Xg, 128, metric=name)
+    G1 = B.robust_prune(Xg, cand, cd, 64, alpha=1.2, metric=name)
+    tc = B.add_reverse(Xg, G1, 64, alpha=1.2, metric=name, method="tc")
+    simt = B.add_reverse(Xg, G1, 64, alpha=1.2, metric=name, method="simt")
+    assert torch.equal(tc, simt)
+    metric = 0 if name == "ip" else 1
+    want = O.add_reverse(X, G1.cpu().numpy(), 64, 1.2, 64, metric, threads=O.cpu_count())
+    assert np.array_equal(tc.cpu().numpy(), want)
+
+
+def test_tensor_core_prune_caps_and_protection():
+    """Per-node degree caps and protected pairs (the offline builder's
+    options) through the tensor-core prune: the CUDA-core prune's output."""
+    X = cases.build_corpus(1500, 96, seed=8, metric=0)
+    Xg = torch.from_numpy(X).to(DEV)
+    cand, cd = B.knn_candidates(Xg, 100, metric="ip")
+    rng = np.random.default_rng(1)
+    dpn = torch.from_numpy(rng.integers(8, 48, 1500).astype(np.int32)).to(DEV)
+    prot = torch.from_numpy(rng.random((1500, 100)) < 0.05).to(DEV)
+    a = B.robust_prune(Xg, cand, cd, 48, deg_per_node=dpn, protect=prot, metric="ip", method="tc")
+    b = B.robust_prune(Xg, cand, cd, 48, deg_per_node=dpn, protect=prot, metric="ip", method="simt")
+    assert torch.equal(a, b)
