@@ -7,9 +7,9 @@ Drop-in for swann/build.py (geniussyn/SWANN): `pairwise`, `knn_candidates`,
                   is scored against the whole corpus and each row's C nearest
                   are selected by swb_topc_block (native); the dot products of
                   the chunk come from a tensor-core GEMM.
-  robust_prune    swb_prune_tc: one block per node, the candidates' Gram
-                  matrix on the tensor cores, the reference's sequential keep
-                  rule (swb_prune: the same on CUDA cores).
+  robust_prune    swb_prune_tc (inner product): one block per node, the
+                  candidates' Gram matrix on the tensor cores, the reference's
+                  sequential keep rule; swb_prune (l2): the same on CUDA cores.
   add_reverse     swb_reverse_tc: stable radix sort of the edges by target, row
                   merge + scoring, then the same prune.
 
@@ -107,8 +107,14 @@ class TcOperands:
             raise N.SwannError(int(self.status[0]), "a device-side wait timed out in the tensor-core prune")
 
 
-def _prune_method(method):
-    method = method or os.environ.get("SWB_PRUNE", "tc")
+def _prune_method(method, metric):
+    """"tc" or "simt".  By default the tensor cores for inner product and the
+    CUDA cores for l2: the l2 pair distance (|x|^2 - 2<x, y>) + |y|^2 cancels
+    (|x|^2 + |y|^2 far above the distance on unnormalised rows), so the
+    tensor-core Gram's error bound, which scales with |x||y|, sends a large
+    share of the pairs to the exact recompute (C5: 2.7 s against 1.6 s on CUDA
+    cores, measured).  Both give the same graph."""
+    method = method or os.environ.get("SWB_PRUNE") or ("tc" if _m(metric) == METRIC_IP else "simt")
     if method not in ("tc", "simt"):
         raise ValueError("prune method must be 'tc' or 'simt'")
     return method
@@ -207,8 +213,9 @@ def robust_prune(Xg, cand, cdist, deg, alpha=1.2, chunk=4096, deg_per_node=None,
     `protect` (bool [n, C], e.g. mutual_rank's) exempts a candidate from the
     detour test.  method "tc" (default; SWB_PRUNE overrides): pair distances
     on the tensor cores, `ops` (TcOperands) prepared once per corpus; "simt":
-    on CUDA cores.  Both give the same graph, bit for bit."""
-    method = _prune_method(method)
+    on CUDA cores.  Both give the same graph, bit for bit; the default is
+    "tc" for inner product and "simt" for l2 (see _prune_method)."""
+    method = _prune_method(method, metric)
     Xf = ops.X if (method == "tc" and ops is not None) else Xg.float().contiguous()
     cand = cand.to(torch.int32).contiguous()
     cdist = cdist.float().contiguous()
@@ -250,7 +257,7 @@ def add_reverse(Xg, G, deg, chunk=2048, alpha=1.2, max_in=64, deg_per_node=None,
     rank's block of a sharded build); G is always the whole graph.  With
     `deg_per_node` (int [n]) the caps are per node and the width is their
     largest, as robust_prune writes it.  `method` / `ops` as robust_prune."""
-    method = _prune_method(method)
+    method = _prune_method(method, metric)
     if method == "tc":
         ops = ops or TcOperands(Xg)
     Xf = ops.X if method == "tc" else Xg.float().contiguous()

@@ -321,7 +321,9 @@ __global__ void __launch_bounds__(NT) prune_tc_kernel(const __grid_constant__ Pa
                 const float ex = (P.metric == METRIC_IP) ? (dg + 1.2e-7f * (1.f + fabsf(g)))
                                                           : (2.f * dg + 2.4e-7f * (gii + 2.f * fabsf(g) + gjj));
                 const float tol = P.alpha * ex + 2.4e-7f * (fabsf(di) + fabsf(a));
-                if (fabsf(a - di) > tol) {
+                // a threshold that is not finite (the reverse pass's empty
+                // slots carry +inf) is decided by any finite pair distance alike
+                if (!isfinite(di) || fabsf(a - di) > tol) {
                     if (a <= di) vm[j >> 5] |= 1u << (j & 31);
                 } else {
                     const int slot = atomicAdd(nlist, 1);
