@@ -941,7 +941,7 @@ def run_reference(args):
     metric = 0 if cfg["metric"] == "ip" else 1
     kw = dict(k=cfg["k"], L=op["queue"], B=64, metric=metric, team=16, vec=8 if cfg["half"] else 4,
               stop_eps=op["stop_eps"], kstop=min(cfg["k"], op["queue"]), threads=cores)
-    per = cores * 2
+    per = cores * 16                                       # ~0.3 s of host work a step
     steps = args.warmup + args.steps
     order = sample_rows(Qh.shape[0], per * steps)          # spread over the batch, input order
     times = []
