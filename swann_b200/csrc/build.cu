@@ -405,7 +405,49 @@ __global__ void seg_starts_kernel(const int32_t* __restrict__ skeys, int64_t tot
 // (ties by id), the first `keepn` written as prune candidates.
 constexpr int RV_THREADS = 128;
 
+// <x_v, x_t>-style chains of one entry, in dimension order: xs is the row
+// (fp32, or fp16 holding the same values), xt the target in shared memory.
+// VEC: 16-byte loads (dim a multiple of the vector width, rows aligned).
+template <typename XT, bool VEC>
+__device__ __forceinline__ float entry_dist(const XT* __restrict__ xv, const float* __restrict__ xt, int dim,
+                                            int metric) {
+    float acc = 0.f;
+    if (VEC) {
+        constexpr int V = VecN<XT>::N;
+        const uint4* p = reinterpret_cast<const uint4*>(xv);
+#pragma unroll 4
+        for (int c = 0; c < dim / V; ++c) {
+            float x[V];
+            widen_u4<XT>(__ldg(p + c), x);
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                if (metric == METRIC_IP) {
+                    acc = fmaf(x[e], xt[c * V + e], acc);
+                } else {
+                    const float df = __fsub_rn(x[e], xt[c * V + e]);
+                    acc = fmaf(df, df, acc);
+                }
+            }
+        }
+    } else {
+        for (int k = 0; k < dim; ++k) {
+            const float x = static_cast<float>(__ldg(&xv[k]));
+            if (metric == METRIC_IP) {
+                acc = fmaf(x, xt[k], acc);
+            } else {
+                const float df = __fsub_rn(x, xt[k]);
+                acc = fmaf(df, df, acc);
+            }
+        }
+    }
+    return metric == METRIC_IP ? __fsub_rn(1.f, acc) : acc;
+}
+
+// XS: the element type the candidates' rows are read in (fp16 for an
+// fp16-valued corpus: the same values, half the bytes), at row stride xs.
+template <typename XS, bool VEC>
 __global__ void __launch_bounds__(RV_THREADS) merge_row_kernel(const float* __restrict__ X, int dim,
+                                                              const XS* __restrict__ Xs, int64_t xs,
                                                               const int32_t* __restrict__ G, int deg,
                                                               const int32_t* __restrict__ svals,
                                                               const int64_t* __restrict__ starts, int max_in,
@@ -468,18 +510,7 @@ __global__ void __launch_bounds__(RV_THREADS) merge_row_kernel(const float* __re
             ids[i] = (i < width) ? 0 : 0x7fffffff;   // the reference scores no-entry slots as id 0, +inf
             continue;
         }
-        const float* xv = X + (size_t)v * dim;
-        float acc = 0.f;
-        if (metric == METRIC_IP) {
-            for (int k = 0; k < dim; ++k) acc = fmaf(__ldg(&xv[k]), xt[k], acc);
-            dd[i] = __fsub_rn(1.f, acc);
-        } else {
-            for (int k = 0; k < dim; ++k) {
-                const float df = __fsub_rn(__ldg(&xv[k]), xt[k]);
-                acc = fmaf(df, df, acc);
-            }
-            dd[i] = acc;
-        }
+        dd[i] = entry_dist<XS, VEC>(Xs + (size_t)v * xs, xt, dim, metric);
     }
     __syncthreads();
     // order by (distance, position)
@@ -681,13 +712,28 @@ int reverse_impl(const float* X, int64_t n, int dim, const int32_t* G, int deg, 
     while (Wp < deg + max_in) Wp <<= 1;
     const int smem = Wp * 12 + dim * 4;
     if (smem > abi::max_smem_optin()) return abi::fail(SWB_ERR_SMEM, "reverse merge needs %d B of shared memory", smem);
-    if (smem > 48 * 1024) {
-        e = cudaFuncSetAttribute(merge_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return abi::cuda_fail(e, "cudaFuncSetAttribute(merge_row)");
+    // the candidates' rows: the fp16 operand copy when the tensor-core prune has
+    // one (fp16-valued corpus), else the fp32 rows; 16-byte loads when aligned
+    const bool half = tc.A && tc.a_dtype == SWB_F16;
+    const void* rowsrc = half ? tc.A : (const void*)X;
+    const int64_t stride = half ? tc.adim : dim;
+    const int vw = half ? 8 : 4;
+    const bool vec = dim % vw == 0 && stride % vw == 0 && reinterpret_cast<uintptr_t>(rowsrc) % 16 == 0;
+    auto launch_merge = [&](auto kern, const auto* src) -> int {
+        if (smem > 48 * 1024) {
+            cudaError_t ea = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (ea != cudaSuccess) return abi::cuda_fail(ea, "cudaFuncSetAttribute(merge_row)");
+        }
+        kern<<<(unsigned)rows, RV_THREADS, smem, st>>>(X, dim, src, stride, G, deg, svals, starts, max_in, metric,
+                                                       keepn, n, row0, cand, cdist);
+        return abi::cuda_check("reverse merge launch");
+    };
+    if (half) {
+        const __half* hs = static_cast<const __half*>(rowsrc);
+        rc = vec ? launch_merge(merge_row_kernel<__half, true>, hs) : launch_merge(merge_row_kernel<__half, false>, hs);
+    } else {
+        rc = vec ? launch_merge(merge_row_kernel<float, true>, X) : launch_merge(merge_row_kernel<float, false>, X);
     }
-    merge_row_kernel<<<(unsigned)rows, RV_THREADS, smem, st>>>(X, dim, G, deg, svals, starts, max_in, metric, keepn,
-                                                               n, row0, cand, cdist);
-    rc = abi::cuda_check("reverse merge launch");
     if (rc) return rc;
     const int32_t* dpn = deg_per_node ? deg_per_node + row0 : nullptr;
     if (tc.A)

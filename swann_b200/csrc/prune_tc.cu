@@ -56,7 +56,7 @@ struct Cfg<MODE_F16> {
     static constexpr int KC = 64;        // elements of K per stage (128 bytes a row)
     static constexpr int ESZ = 2;
     static constexpr int NOPS = 1;
-    static constexpr int STAGES = 4;
+    static constexpr int STAGES = 6;     // 96 KB: two CTAs an SM still fit
     static constexpr uint32_t FMT = 0;   // F16
 };
 template <>
