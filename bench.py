@@ -283,12 +283,16 @@ def build_index(cfg, dev, world, rank):
         G1 = B.robust_prune(X, cand, cd, 64, alpha=1.2, metric=cfg["metric"], ops=ops)
         torch.cuda.synchronize()
         t["prune_s"] = time.perf_counter() - t1
+        tp = time.perf_counter()
+        parity = candidate_parity(X, cand, cd, metric=cfg["metric"])   # a check of the sweep's lists, not timed
+        t["parity_s"] = time.perf_counter() - tp
         del cand, cd
         t1 = time.perf_counter()
         G = B.add_reverse(X, G1, 64, alpha=1.2, metric=cfg["metric"], ops=ops)
         torch.cuda.synchronize()
         t["reverse_s"] = time.perf_counter() - t1
         t["exact_recomputed_pairs"] = int(ops.recomputed[0])
+        t["candidate_parity"] = parity
         del ops
     else:
         a, b = D.shard_bounds(n, world)[rank]
@@ -328,7 +332,7 @@ def build_index(cfg, dev, world, rank):
         t.update(stage)
         shared.clear()
     torch.cuda.synchronize()
-    t["total_s"] = time.perf_counter() - t0
+    t["total_s"] = time.perf_counter() - t0 - t.get("parity_s", 0.0)
     return X, G, t
 
 
@@ -705,7 +709,7 @@ def run(args):
         "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": 3 * args.steps,
         "gpu_launches_per_step": "sel::topk_kernel (seed top-E), swb::prepare_kernel (table clear), "
                                  "swb::fused_kernel (search); plus library GEMM/sort/gather launches",
-        "build": {**{k: round(v, 3) for k, v in build_t.items()},
+        "build": {**{k: (round(v, 3) if isinstance(v, float) else v) for k, v in build_t.items()},
                   "roofline": sweep_roofline(build_t, cfg["n"], cfg["d"], cfg["half"]) if world == 1 else None},
         "calibration": [{"branches": b_, "queue": q, "stop_eps": e, "recall": round(r, 4),
                          "ms": None if t is None else round(t, 3)} for b_, q, e, r, t in tried],
