@@ -145,3 +145,14 @@ def test_sharded_build_equals_single_process(tmp_path):
     X = cases.build_corpus(900, 24, seed=3, metric=1)
     want = O.build_graph(X, metric=1, degree=16, candidates=32)
     assert np.array_equal(G, want)
+
+
+def test_bench_corpus_row_blocks_equal_the_whole():
+    """bench.py's seeded generator: the rows a rank generates for its block of a
+    sharded build are exactly those rows of the single-process corpus, at
+    block edges that do not fall on the generator's 65536-row chunks."""
+    import bench
+    full = bench.gen_mixture(150_000, 8, 7, 1, torch.device("cpu"), False, True)
+    for a, b in ((0, 1), (70_000, 140_000), (65_535, 65_537), (131_071, 150_000)):
+        part = bench.gen_mixture(150_000, 8, 7, 1, torch.device("cpu"), False, True, rows=(a, b))
+        assert torch.equal(part, full[a:b]), (a, b)
