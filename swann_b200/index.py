@@ -231,18 +231,18 @@ class Index:
                     src = host if host is not None else queries
                     Qd = src[a:b].to(r.dev, non_blocking=True).float().contiguous()
                     self._search_part(r, Qd, k, cfg, Hc, outs, checks)
-        key_of = lambda r: _claims_key(cfg.branches, cfg.budget, cfg.queue, cfg.stop_eps, r.G.shape[1])  # noqa: E731
         overflow = 0
         for r, ctr in checks:
+            key = _claims_key(cfg.branches, cfg.budget, cfg.queue, cfg.stop_eps, r.G.shape[1])
             # the most table slots one query claimed (its branches' claims plus
             # their seeds), and the visited-table overflow count
             claims = (ctr[..., 5].to(torch.int64).sum(1) + ctr.shape[1]).max()
             if E._OVERFLOW_GUARD:
                 fails, most = torch.stack([ctr[..., 2].to(torch.int64).sum(), claims]).tolist()
                 overflow += fails
-                self._note_claims(key_of(r), claims, host_value=most)
+                self._note_claims(key, claims, host_value=most)
             else:
-                self._note_claims(key_of(r), claims)
+                self._note_claims(key, claims)
         if overflow:
             raise RuntimeError("visited table overflowed: raise the budget used for sizing")
         dev0 = reps[0].dev

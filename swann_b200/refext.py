@@ -35,6 +35,8 @@ import torch
 from . import _lib as N
 
 FLT_MAX_BITS = 0x7F7FFFFF
+N_CTR = 10          # counters per branch (local_search.cu:35-41)
+N_METRIC_IP = 0
 
 
 class _Scratch:
@@ -222,6 +224,3 @@ def merge_branches(bids, bdist, k):
     _check(rc, "merge_branches")
     return [oi, od]
 
-
-N_CTR = 10
-N_METRIC_IP = 0
