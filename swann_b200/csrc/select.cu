@@ -10,12 +10,16 @@
 // One warp per query row.  The row's list (at most 32 * R entries, sorted by
 // (distance, index)) lives in shared memory; each lane reads four scores at a
 // time, values that cannot enter the list are dropped against its E-th key,
-// and each group of 32 candidates that has a survivor is sorted across the
-// warp and merged: every entry's new position is its own index plus the number
-// of entries of the other sequence before it (binary lifting over the lanes),
-// so both sequences are scattered straight into the other half of a ping-pong
-// pair.  Ties between equal distances go to the lower index; torch.topk leaves
-// that order unspecified.
+// and the survivors are buffered in shared memory; each time 32 have gathered
+// they are sorted across the warp and merged: every entry's new position is
+// its own index plus the number of entries of the other sequence before it
+// (binary lifting over the lanes), so both sequences are scattered straight
+// into the other half of a ping-pong pair.  (A row of 4096 scores has about
+// 155 survivors against a running E = 32: buffering merges them in ~5-10
+// rounds rather than once per 32-column group that holds one.)  The filter
+// only drops keys that cannot be in the final list, so the result does not
+// depend on when the merges happen.  Ties between equal distances go to the
+// lower index; torch.topk leaves that order unspecified.
 
 #include <cstdint>
 
@@ -128,6 +132,8 @@ __global__ void __launch_bounds__(WARPS * 32) topk_kernel(const float* __restric
                                                           int resume, int vec) {
     __shared__ float s_d[WARPS][2][32 * R];
     __shared__ int s_i[WARPS][2][32 * R];
+    __shared__ float b_d[WARPS][64];   // survivors waiting for a merge (at most 63)
+    __shared__ int b_i[WARPS][64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * WARPS + warp;
     if (row >= rows) return;   // whole warps only: nothing below synchronises the block
@@ -153,6 +159,7 @@ __global__ void __launch_bounds__(WARPS * 32) topk_kernel(const float* __restric
         thi = s_i[warp][cur][E - 1];
     }
     const float q2 = (metric == METRIC_L2) ? qn[row] : 0.f;
+    int cnt = 0;   // buffered survivors
     const float* srow = S + row * ld;
     for (int c0 = 0; c0 < P; c0 += 128) {
         const int jb = c0 + 4 * lane;
@@ -174,15 +181,38 @@ __global__ void __launch_bounds__(WARPS * 32) topk_kernel(const float* __restric
         for (int u = 0; u < 4; ++u) {
             const int j = col0 + jb + u;
             const bool keep = (jb + u < P) && (nb < E || key_lt(d[u], j, thd, thi));
-            if (!__any_sync(FULL, keep)) continue;
-            nb = merge32<R>(s_d[warp][cur], s_i[warp][cur], s_d[warp][cur ^ 1], s_i[warp][cur ^ 1], nb, E,
-                            keep ? d[u] : INF, keep ? j : 0x7fffffff, lane);
-            cur ^= 1;
-            if (nb == E) {
-                thd = s_d[warp][cur][E - 1];
-                thi = s_i[warp][cur][E - 1];
+            const unsigned km = __ballot_sync(FULL, keep);
+            if (!km) continue;
+            if (keep) {
+                const int pos = cnt + __popc(km & lanemask_lt());
+                b_d[warp][pos] = d[u];
+                b_i[warp][pos] = j;
+            }
+            cnt += __popc(km);
+            __syncwarp();
+            if (cnt >= 32) {   // merge 32 buffered survivors, keep the rest
+                nb = merge32<R>(s_d[warp][cur], s_i[warp][cur], s_d[warp][cur ^ 1], s_i[warp][cur ^ 1], nb, E,
+                                b_d[warp][lane], b_i[warp][lane], lane);
+                cur ^= 1;
+                const float rd = (lane + 32 < cnt) ? b_d[warp][lane + 32] : INF;
+                const int ri = (lane + 32 < cnt) ? b_i[warp][lane + 32] : 0x7fffffff;
+                __syncwarp();
+                b_d[warp][lane] = rd;
+                b_i[warp][lane] = ri;
+                cnt -= 32;
+                __syncwarp();
+                if (nb == E) {
+                    thd = s_d[warp][cur][E - 1];
+                    thi = s_i[warp][cur][E - 1];
+                }
             }
         }
+    }
+    if (cnt > 0) {   // the last survivors (fewer than 32; the rest of the lanes offer nothing)
+        const bool ok = lane < cnt;
+        nb = merge32<R>(s_d[warp][cur], s_i[warp][cur], s_d[warp][cur ^ 1], s_i[warp][cur ^ 1], nb, E,
+                        ok ? b_d[warp][lane] : INF, ok ? b_i[warp][lane] : 0x7fffffff, lane);
+        cur ^= 1;
     }
     for (int e = lane; e < E; e += 32) {
         const bool ok = e < nb;
