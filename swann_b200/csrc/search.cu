@@ -695,12 +695,19 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             nk += __popc(km);
         }
         __syncwarp();
+        int fanout_extra = 0;
         if (CODES && limit != FLT_MAX && m > 0) {
             int skipped = 0;
             m = code_filter<TEAM, XT>(K, w, m, sq, limit, qmu, qsum, lane, skipped);
             claimed_rows = 0;   // recounted below from the rows actually scored
             for (int b = 0; b < m; b += 32)
                 claimed_rows += __popc(__ballot_sync(FULL, b + lane < m && w.w_slot[b + lane] >= 0));
+            // The reference keeps a skipped neighbour as a candidate at distance
+            // FLT_MAX (local_search.cu:574-585), admitted by the keep test only
+            // while the queue's last slot is empty -- where the queue's empty
+            // slots, (FLT_MAX, -1), sort before it, so it never enters the queue.
+            // Its one trace is the fan-out count (counter 8), kept here too.
+            if (worst == FLT_MAX) fanout_extra = skipped;
         }
         score_rows<TEAM, XT>(K, w, m, sq, ctab, lane);
         for (int b = 0; b < m; b += 32) {
@@ -726,7 +733,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
         ctr.add(lane, 2, fails);
         ctr.add(lane, 4, hits);
         ctr.add(lane, 5, claimed_rows);
-        ctr.add(lane, 8, nk);
+        ctr.add(lane, 8, nk + fanout_extra);
         ctr.add(lane, 9, 1);
         __syncwarp();
         if (nk > 0) {
