@@ -778,7 +778,7 @@ def tensor_peaks(seconds=3.0, n=8192):
     return out
 
 
-def candidate_parity(X, cand, cdist, rows=256, rel=1e-6, metric="l2"):
+def candidate_parity(X, cand, cdist, rows=256, rel=1e-6, metric="l2", chunk=1 << 20):
     """Build parity at full size, for a sample of rows spread over the corpus:
     the sweep's candidate lists against the exact ones (every column, float64,
     the reference's expressions), and -- as the baseline the 1e-6 rule is held
@@ -788,57 +788,71 @@ def candidate_parity(X, cand, cdist, rows=256, rel=1e-6, metric="l2"):
     two ids' exact distances differ by at most `rel` relative; every other
     difference is a mismatch.  Also: the same count against the reference's
     lists directly, and the largest relative gap between a list's own fp32
-    distance and the exact one."""
+    distance and the exact one.  Columns are streamed in chunks with a running
+    top list, so nothing of the corpus's size is held in float64."""
     n, C = cand.shape
     dev = X.device
     pick = torch.from_numpy(sample_rows(n, rows)).to(dev)
-    X64 = X.double()
-    xn64 = (X64 * X64).sum(1)
-    A64 = X64[pick]
-    dots = A64 @ X64.T
-    D = 1.0 - dots if metric == "ip" else (xn64[None, :] - 2.0 * dots + xn64[pick][:, None]).clamp(min=0)
-    del dots
-    D[torch.arange(len(pick), device=dev), pick] = 3.4e38
-    # exact lists in (distance, id) order
-    ed, ei = torch.topk(D, C + 8, dim=1, largest=False)
-    order = torch.from_numpy(np.lexsort((ei.cpu().numpy(), ed.cpu().numpy()), axis=1)).to(dev)
-    ei = torch.gather(ei, 1, order)[:, :C]
-    del ed
-    # the reference's fp32 arithmetic
+    m = len(pick)
+    A64 = X[pick].double()
+    an64 = (A64 * A64).sum(1)
+    Af = X[pick].float()
+    an32 = (Af * Af).sum(1)
+    ar = torch.arange(m, device=dev)
+    best = [None, None]    # exact: distances, ids (running, (C + 8) per row)
+    refb = [None, None]    # the reference's fp32 arithmetic
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        Xf = X.float()
-        Af = Xf[pick]
-        s32 = Af @ Xf.T
-        if metric == "ip":
-            R = 1.0 - s32
-        else:
-            bn = (Xf * Xf).sum(1)
-            R = (bn.view(1, -1) - 2.0 * s32 + (Af * Af).sum(1).view(-1, 1)).clamp(min=0)
-        del s32
-        R[torch.arange(len(pick), device=dev), pick] = 3.4e38
-        rd, ri = torch.topk(R, C, dim=1, largest=False)
-        del R
+        for c0 in range(0, n, chunk):
+            c1 = min(n, c0 + chunk)
+            Xc = X[c0:c1]
+            X64 = Xc.double()
+            dots = A64 @ X64.T
+            D = 1.0 - dots if metric == "ip" else (((X64 * X64).sum(1))[None, :] - 2.0 * dots + an64[:, None]).clamp(min=0)
+            Xf = Xc.float()
+            s32 = Af @ Xf.T
+            R = 1.0 - s32 if metric == "ip" else ((Xf * Xf).sum(1)[None, :] - 2.0 * s32 + an32[:, None]).clamp(min=0)
+            inside = (pick >= c0) & (pick < c1)
+            D[ar[inside], pick[inside] - c0] = 3.4e38
+            R[ar[inside], pick[inside] - c0] = 3.4e38
+            for acc, M, kk in ((best, D, C + 8), (refb, R, C)):
+                v, i = torch.topk(M, min(kk, c1 - c0), dim=1, largest=False)
+                i = i + c0
+                if acc[0] is not None:
+                    v, j = torch.topk(torch.cat([acc[0], v], 1), kk, dim=1, largest=False)
+                    i = torch.gather(torch.cat([acc[1], i], 1), 1, j)
+                acc[0], acc[1] = v, i
+            del dots, D, R, X64, Xf, s32
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
-    mine = cand[pick].long()
+    ed, ei = best
+    order = torch.from_numpy(np.lexsort((ei.cpu().numpy(), ed.cpu().numpy()), axis=1)).to(dev)
+    ei = torch.gather(ei, 1, order)[:, :C]
+    rd, ri = refb
 
-    def compare(got, want):
-        dg = torch.gather(D, 1, got)
-        dw = torch.gather(D, 1, want)
+    def exact(ids):
+        """exact distances of the rows' listed ids (float64)"""
+        V = X[ids.reshape(-1)].double().view(m, C, -1)
+        if metric == "ip":
+            return 1.0 - (V * A64[:, None, :]).sum(-1)
+        return ((V - A64[:, None, :]) ** 2).sum(-1)
+
+    d_ex, d_ref = exact(ei), exact(ri)
+    mine = cand[pick].long()
+    d_mine = exact(mine)
+
+    def compare(got, dg, want, dw):
         diff = got != want
         tie = (dg - dw).abs() <= rel * dw.abs()
         return int((diff & ~tie).sum()), int((diff & tie).sum())
 
-    m_ex, t_ex = compare(mine, ei)
-    r_ex, rt_ex = compare(ri, ei)
-    m_ref, t_ref = compare(mine, ri)
-    ex_mine = torch.gather(D, 1, mine)
-    gap_mine = float(((cdist[pick].double() - ex_mine).abs() / ex_mine.abs().clamp(min=1e-30)).max())
-    ex_ref = torch.gather(D, 1, ri)
-    gap_ref = float(((rd.double() - ex_ref).abs() / ex_ref.abs().clamp(min=1e-30)).max())
-    return {"rows_checked": int(len(pick)), "positions": int(len(pick) * C), "tie_rule": f"exact distances within {rel:g} relative",
+    m_ex, t_ex = compare(mine, d_mine, ei, d_ex)
+    r_ex, rt_ex = compare(ri, d_ref, ei, d_ex)
+    m_ref, t_ref = compare(mine, d_mine, ri, d_ref)
+    gap_mine = float(((cdist[pick].double() - d_mine).abs() / d_mine.abs().clamp(min=1e-30)).max())
+    gap_ref = float(((rd.double() - d_ref).abs() / d_ref.abs().clamp(min=1e-30)).max())
+    return {"rows_checked": int(m), "positions": int(m * C), "tie_rule": f"exact distances within {rel:g} relative",
             "vs_exact": {"non_tie_mismatches": m_ex, "tie_swaps": t_ex},
             "reference_fp32_vs_exact": {"non_tie_mismatches": r_ex, "tie_swaps": rt_ex},
             "vs_reference_fp32": {"non_tie_mismatches": m_ref, "tie_swaps": t_ref},
