@@ -586,7 +586,26 @@ def run(args):
             checks[f"recall@{cfg['k']}"] = round(recall(got, truth, cfg["k"]), 4)
         checks["max_rel_dist_err"] = exact_distance_error(X, Qall[:gt_n], ids_s, dist_s, cfg["metric"])
 
+    # With several GPUs, each step shards the global batch by locality: every
+    # rank orders the whole batch along the catalogue tour (Index.route, the
+    # same order on every rank) and searches its contiguous slice of that order.
+    routed = world > 1 and not args.positional and index.route(Qall) is not None
+    if routed:
+        import torch.distributed as dist
+        o = index.route(Qall)
+        sig = torch.tensor([float((o[:4096].double() * torch.arange(4096, device=dev)).sum()), float(o.sum())],
+                           dtype=torch.float64, device=dev)
+        lo, hi = sig.clone(), sig.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        if not torch.equal(lo, hi):
+            raise RuntimeError("ranks disagree on the routed order; run with --positional")
+        Q = Qall[o[a:b]].contiguous()   # this rank's routed shard (for the roofline leg)
+
     def step():
+        if routed:
+            order = index.route(Qall)
+            return index.search_tensors(Qall[order[a:b]], k=cfg["k"], **op)
         return index.search_tensors(Q, k=cfg["k"], **op)
 
     # -- device-resident timing (value): strong scaling, the global batch split
@@ -596,7 +615,7 @@ def run(args):
     # -- weak scaling beside it (N > 1): a full batch on every GPU ----------
     weak = None
     if world > 1:
-        Qw = make_queries(cfg, dev, 2000 + rank, batch)
+        Qw = make_queries(cfg, dev, 2000 + rank, batch)   # a whole batch per GPU: nothing to route
         ms_w, _ = timed_steps(lambda: index.search_tensors(Qw, k=cfg["k"], **op), args.steps, args.warmup, world,
                               local, sample_clocks=False)
         weak = {"value": round(world * batch * args.steps / (ms_w / 1e3), 1), "unit": "queries/s",
@@ -604,7 +623,8 @@ def run(args):
         del Qw
 
     # -- end to end through the public API with host buffers -------------
-    Qh = Q.cpu().pin_memory()
+    # host batches are sharded by position (routing needs the batch on a GPU)
+    Qh = Qall[a:b].cpu().pin_memory()
     for _ in range(max(1, args.warmup // 2)):
         index.search(Qh, k=cfg["k"], **op)
     torch.cuda.synchronize()
@@ -617,7 +637,8 @@ def run(args):
     e2e = {"value": round(batch * args.steps / e2e_s, 1), "unit": "queries/s",
            "h2d_bytes_per_step": int(Qh.numel() * Qh.element_size()),
            "d2h_bytes_per_step": int(out_ids.nbytes + out_d.nbytes),
-           "timing": "wall clock, host pinned queries to numpy answers, max over ranks"}
+           "timing": "wall clock, host pinned queries to numpy answers, max over ranks",
+           "sharding": "contiguous slices of the global batch"}
 
     # -- roofline of the dominant kernel (the fused search) on this rank's shard
     nq = Q.shape[0]
@@ -705,7 +726,10 @@ def run(args):
                    "query_order": "nearest catalogue entry" if index.locality else "input",
                    "l2": "inputs larger than L2 (corpus %.1f GB; rows gathered at random)" % (
                        X.numel() * X.element_size() / 1e9),
-                   "parallelism": f"query shards x{world}, replicas"},
+                   "parallelism": f"query shards x{world}, replicas",
+                   "sharding": ("by locality: each step orders the global batch along the catalogue tour "
+                                "(Index.route, timed) and each rank searches its slice" if routed else
+                                "contiguous slices of the global batch")},
         "e2e": e2e, "roofline": roofline, "clocks": clocks, "gpu_launches": 3 * args.steps,
         "gpu_launches_per_step": "sel::topk_kernel (seed top-E), swb::prepare_kernel (table clear), "
                                  "swb::fused_kernel (search); plus library GEMM/sort/gather launches",
@@ -1068,6 +1092,7 @@ def main():
     ap.add_argument("--gt", type=int, default=8192)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (and build parity) legs")
     ap.add_argument("--no-ref", action="store_true", help="skip the reference-kernel leg")
+    ap.add_argument("--positional", action="store_true", help="N > 1: shard the batch by position, not locality")
     ap.add_argument("--fixed", default="", help="branches,queue,stop_eps: skip the calibration")
     ap.add_argument("--build-only", action="store_true", help="time the graph build instead of the search")
     ap.add_argument("--batch-sweep", action="store_true", help="QPS and latency across the C3 batch sizes")

@@ -9,8 +9,10 @@ Drop-in for swann/index.py (geniussyn/SWANN):
 Same constructor, `build`, `search(queries, k, config, **overrides)`, `save`,
 `load`, `SearchConfig` defaults and errors.  One addition: `devices=[...]`
 replicates the corpus, graph and catalogue on several GPUs and splits each
-query batch across them in contiguous shards -- queries are independent, so
-the shards need no communication and the results are concatenated in order.
+query batch across them -- queries are independent, so the shards need no
+communication and the results come back in input order.  A device-resident
+batch is split by locality (`Index.route`: each shard one stretch of the
+catalogue's tour); a host batch in contiguous slices.
 """
 from __future__ import annotations
 
@@ -108,8 +110,10 @@ class Index:
         self._replicas = [_Replica(self.X, self.G, self.catalogue, d) for d in devs]
         self._cat = self._replicas[0].cat_rows
         self._tour = _catalogue_tour(self._cat, self._m) if self.locality else None
+        lm = _landmarks(self._cat, self._tour) if self._tour is not None else None
         for r in self._replicas:
             r.tour = None if self._tour is None else self._tour.to(r.dev)
+            r.landmarks = None if lm is None else tuple(t.to(r.dev) for t in lm)
         # Slots of each query's distance table.  A power of two fixes it.
         # None (the default) sizes it from what the queries claim: the first
         # search of a configuration uses the reference's sizing
@@ -129,6 +133,29 @@ class Index:
     @property
     def devices(self):
         return [r.dev for r in self._replicas]
+
+    # -- sharding by locality -------------------------------------------------
+    def route(self, queries: torch.Tensor):
+        """An order of a device-resident batch along the catalogue's locality
+        tour (int64, on the queries' device), or None without a tour: equal
+        contiguous slices of it are query shards whose members sit in one
+        stretch of the tour.  Each query goes to its nearest of LANDMARKS
+        catalogue entries spread evenly along the tour (a TF32 GEMM against
+        them, the arithmetic select_nearest uses); ties keep input order.  A
+        GPU searching such a shard walks a fraction of the graph with as many
+        queries per region as one GPU searching the whole batch, so queries
+        running side by side share rows in L2.  The order depends only on the
+        batch and the index, so every process computing it gets the same one."""
+        if self._tour is None or queries.shape[0] == 0:
+            return None
+        r = next((x for x in self._replicas if x.dev == queries.device), self._replicas[0])
+        lm_rows, lm_keys, lm_norms = r.landmarks
+        Q = queries.to(r.dev).float()
+        with S.reduced_precision(True):
+            sc = Q @ lm_rows.T
+        near = torch.argmax(sc, dim=1) if self._m == METRICS["ip"] else torch.argmin(lm_norms[None, :] - 2.0 * sc, 1)
+        order = torch.argsort(lm_keys[near], stable=True)
+        return order.to(queries.device)
 
     # -- per-query table size ------------------------------------------------
     def table_slots_for(self, branches, budget, queue, stop_eps, degree) -> int:
@@ -194,6 +221,9 @@ class Index:
         host = queries if not isinstance(queries, torch.Tensor) or queries.device.type == "cpu" else None
         if host is not None and isinstance(host, np.ndarray):
             host = torch.from_numpy(np.ascontiguousarray(host))
+        # Several GPUs and a device-resident batch: shards by locality (route);
+        # host batches keep contiguous shards, each copied over its own GPU's link.
+        order = self.route(queries) if (len(reps) > 1 and host is None) else None
         outs, checks = [], []
         for r, (a, b) in zip(reps, zip(bounds[:-1], bounds[1:])):
             if b <= a:
@@ -229,7 +259,8 @@ class Index:
                     self._search_part(r, Qd, k, cfg, Hc, outs, checks, ent=torch.cat(ents))
                 else:
                     src = host if host is not None else queries
-                    Qd = src[a:b].to(r.dev, non_blocking=True).float().contiguous()
+                    part = src[a:b] if order is None else src[order[a:b]]
+                    Qd = part.to(r.dev, non_blocking=True).float().contiguous()
                     self._search_part(r, Qd, k, cfg, Hc, outs, checks)
         overflow = 0
         for r, ctr in checks:
@@ -248,6 +279,11 @@ class Index:
         dev0 = reps[0].dev
         ids = torch.cat([o[0].to(dev0) for o in outs]) if outs else torch.empty((0, k), dtype=torch.int32)
         dist = torch.cat([o[1].to(dev0) for o in outs]) if outs else torch.empty((0, k))
+        if order is not None:   # back to input order
+            back = order.to(dev0)
+            ids_in, dist_in = torch.empty_like(ids), torch.empty_like(dist)
+            ids_in[back], dist_in[back] = ids, dist
+            ids, dist = ids_in, dist_in
         return ids, dist
 
     def _search_part(self, r, Qd, k, cfg, Hc, outs, checks, ent=None):
@@ -344,6 +380,20 @@ TOUR_MAX = 16384
 # busiest query seen, ~15% for a typical one at C3)
 TABLE_HEADROOM = 1.5
 TABLE_MIN = 4096
+
+
+# catalogue entries a batch is routed by when it is sharded over several GPUs
+LANDMARKS = 256
+
+
+def _landmarks(cat_rows, tour, count=LANDMARKS):
+    """LANDMARKS catalogue entries spread evenly along the tour: their rows
+    (fp32), their tour positions and their squared norms."""
+    P = cat_rows.shape[0]
+    by_pos = torch.argsort(tour.to(cat_rows.device))
+    pick = by_pos[torch.linspace(0, P - 1, min(count, P), device=cat_rows.device).round().long()]
+    rows = cat_rows[pick].float().contiguous()
+    return rows, tour.to(cat_rows.device)[pick].contiguous(), (rows * rows).sum(1).contiguous()
 
 
 def _claims_key(branches, budget, queue, stop_eps, degree):

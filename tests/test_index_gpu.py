@@ -160,3 +160,42 @@ def test_locality_order_returns_answers_in_input_order(ip_index):
     assert abs(recall(ids_on[sample], truth, 10) - recall(ids_off[sample], truth, 10)) < 0.01
     # most queries get the very same answer either way (the branch race aside)
     assert np.mean((ids_on == ids_off).all(1)) > 0.9
+
+
+def test_route_orders_a_batch_along_the_tour(ip_index):
+    """Index.route: a permutation of the batch whose landmark keys (tour
+    positions of each query's nearest landmark) never decrease, and the same
+    order on a second call."""
+    X, Q, index = ip_index
+    rng = np.random.default_rng(3)
+    Qb = rng.standard_normal((3000, X.shape[1]), dtype=np.float32)
+    Qb /= np.linalg.norm(Qb, axis=1, keepdims=True)
+    Qg = torch.from_numpy(Qb).cuda()
+    order = index.route(Qg)
+    assert order is not None
+    o = order.cpu().numpy()
+    assert np.array_equal(np.sort(o), np.arange(3000))
+    rows, keys, _ = index._replicas[0].landmarks
+    near = torch.argmax(Qg @ rows.T, dim=1)
+    k = keys[near].cpu().numpy()[o]
+    assert (np.diff(k) >= 0).all()
+    assert torch.equal(order, index.route(Qg))
+
+
+def test_routed_replicas_answer_in_input_order(ip_index):
+    """Two replicas (here on one GPU) split a device-resident batch by
+    locality: every answer comes back at its query's input position with its
+    exact distance, and the recall matches one replica's."""
+    X, Q, index = ip_index
+    two = swann.Index(index.X, index.G, metric="ip", catalogue=index.catalogue, devices=[0, 0])
+    rng = np.random.default_rng(4)
+    Qb = rng.standard_normal((2048, X.shape[1]), dtype=np.float32)
+    Qb /= np.linalg.norm(Qb, axis=1, keepdims=True)
+    Qg = torch.from_numpy(Qb).cuda()
+    ids2, dist2 = two.search_tensors(Qg, k=10, branches=16)
+    ids1, _ = index.search_tensors(Qg, k=10, branches=16)
+    ids2, dist2 = ids2.cpu().numpy(), dist2.cpu().numpy()
+    ex = 1.0 - np.einsum("qkd,qd->qk", X[ids2].astype(np.float64), Qb.astype(np.float64))
+    assert np.allclose(dist2, ex, atol=2e-6)
+    truth = exact(X, Qb, 10, "ip")
+    assert abs(recall(ids2, truth, 10) - recall(ids1.cpu().numpy(), truth, 10)) <= 0.01
