@@ -234,9 +234,9 @@ def dist_setup():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # NCCL's version banner goes to stdout; rank 0's stdout carries only the JSON line
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL writes its version banner (and warnings) to stdout unless given a
+        # file; rank 0's stdout carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", f"/tmp/swb_nccl_{os.getpid()}.log")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
