@@ -598,9 +598,9 @@ def run(args):
         lo, hi = sig.clone(), sig.clone()
         dist.all_reduce(lo, op=dist.ReduceOp.MIN)
         dist.all_reduce(hi, op=dist.ReduceOp.MAX)
-        if not torch.equal(lo, hi):
-            raise RuntimeError("ranks disagree on the routed order; run with --positional")
-        Q = Qall[o[a:b]].contiguous()   # this rank's routed shard (for the roofline leg)
+        routed = bool(torch.equal(lo, hi))   # every rank sees the same verdict; else contiguous slices
+        if routed:
+            Q = Qall[o[a:b]].contiguous()   # this rank's routed shard (for the roofline leg)
 
     def step():
         if routed:
