@@ -1025,6 +1025,21 @@ def run_reference(args):
 BATCH_SWEEP = [(1, 128), (8, 128), (64, 128), (512, 64), (4096, 32), (65535, 32)]
 
 
+def wall_per_batch(call, b, nmax, reps):
+    """Median wall-clock seconds of one synchronous call(a) over consecutive
+    slices [a, a + b) of an nmax-query set, after one untimed call."""
+    call(0)
+    torch.cuda.synchronize()
+    ts = []
+    for i in range(reps):
+        a = ((i + 1) * b) % (nmax - b + 1)
+        t = time.perf_counter()
+        call(a)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t)
+    return statistics.median(ts)
+
+
 def run_batch_sweep(args):
     """QPS and per-batch latency across batch sizes on one GPU, one index.
     The operating point per branch count is the smallest stop_eps (queue 12)
@@ -1069,14 +1084,42 @@ def run_batch_sweep(args):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
+        wall = wall_per_batch(lambda a: index.search(Q[a:a + b], **kw), b, nmax, min(reps, 50))
         rows.append({"batch": b, "branches": br, "queue": 12, "stop_eps": eps, "recall@10": round(r, 4),
                      "table_slots": slots,
-                     "ms_per_batch": round(ms, 3), "qps": round(b / (ms / 1e3), 1), "batches_timed": reps})
+                     "ms_per_batch": round(ms, 3), "qps": round(b / (ms / 1e3), 1), "batches_timed": reps,
+                     "wall_ms_per_batch": round(wall * 1e3, 3)})
+    swann_ref = None if args.no_ref else reference_package()
+    if swann_ref is not None:
+        # the reference's own Index.search on the same graph, catalogue and
+        # operating points, timed like `wall_ms_per_batch` above
+        impl = reference_kernels_for(swann_ref)
+        ref_index = swann_ref.Index(X, G, metric=cfg["metric"], catalogue=index.catalogue)
+        ref_recall = {}
+        for row in rows:
+            kw = dict(k=cfg["k"], branches=row["branches"], queue=12, stop_eps=row["stop_eps"])
+            key = (row["branches"], row["stop_eps"])
+            if key not in ref_recall:
+                ids, _ = ref_index.search(Q[:gt_n], **kw)
+                ref_recall[key] = recall(ids[:, :10], truth[:, :10], 10)
+            b = row["batch"]
+            sec = wall_per_batch(lambda a: ref_index.search(Q[a:a + b], **kw), b, nmax,
+                                 max(3, min(50, nmax // b)))
+            row["reference"] = {"wall_ms_per_batch": round(sec * 1e3, 3), "qps": round(b / sec, 1),
+                                "recall@10": round(ref_recall[key], 4)}
+        del ref_index
+        torch.cuda.empty_cache()
+    else:
+        impl = None
     line = {"metric": f"QPS and latency by batch size at recall@10>={TARGET} ({cfg['desc']})",
             "unit": "queries/s", "n_gpus": 1, "higher_is_better": True, "dtype": "f32",
             "data": "synthetic (seeded Gaussian mixture generated on the GPU, BASELINE.json config)",
             "config": {"workload": args.config, "n": cfg["n"], "d": cfg["d"], "k": cfg["k"], "budget": 64,
-                       "team": 16, "recall_sample": gt_n, "timing": "CUDA events, device-resident queries"},
+                       "team": 16, "recall_sample": gt_n,
+                       "timing": "ms_per_batch: CUDA events over back-to-back calls, device-resident queries; "
+                                 "wall_ms_per_batch: median wall clock of one synchronous Index.search call "
+                                 "(device-resident queries, numpy answers), the reference timed the same way"},
+            "reference": impl or "not run (--no-ref, or the reference package is not installed)",
             "batches": rows}
     print(json.dumps(line), flush=True)
 

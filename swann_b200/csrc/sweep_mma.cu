@@ -389,8 +389,8 @@ __device__ __noinline__ RowState flush_rows(const Params& P, const float* bufd, 
 // every value below the row's threshold goes to the row's buffer.  Ids already
 // merged into the row's best list are all below j0, so the (distance, id) key
 // order reduces to the distance alone here.  The common case -- nothing in the
-// group beats the threshold on any lane of the warp -- costs the 16 distances,
-// a balanced min tree and one vote.  Otherwise each kept value is stored at
+// group beats the threshold on any lane of the warp -- costs a balanced
+// max (IP) or min (L2, after the 16 distances) tree and one vote.  Otherwise each kept value is stored at
 // cnt + (kept values before it), in column order, so a discarded value's store
 // is overwritten by the next kept one (positions stay below cnt + 16 <= BUF: a
 // group starts at cnt <= BUF - GROUP).  Returns whether any lane of the warp
@@ -400,23 +400,47 @@ template <int METRIC, bool TAIL>
 __device__ __forceinline__ bool filter16(const float* v, const float* nrm, float an, int j0, int lim, float th,
                                          int& cnt, float* myd, int* myi) {
     float d[16];
+    float mn;
+    if (METRIC == METRIC_IP) {
+        // 1 - v is non-increasing in v and rounding is monotone, so the group's
+        // smallest distance is 1 - (its largest similarity), NaNs ignored by
+        // both forms: one subtraction on the common path instead of sixteen.
+        float m[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        if (METRIC == METRIC_IP) {
-            d[i] = __fsub_rn(1.f, v[i]);
-        } else {
-            float e = __fadd_rn(__fsub_rn(nrm[i], __fmul_rn(2.f, v[i])), an);
-            d[i] = e < 0.f ? 0.f : e;
+        for (int i = 0; i < 8; ++i) {
+            const float a = (TAIL && 2 * i >= lim) ? __int_as_float(0xff800000) : v[2 * i];
+            const float b = (TAIL && 2 * i + 1 >= lim) ? __int_as_float(0xff800000) : v[2 * i + 1];
+            m[i] = fmaxf(a, b);
         }
-        if (TAIL && i >= lim) d[i] = __int_as_float(0x7f800000);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[2 * i], m[2 * i + 1]);
+        mn = __fsub_rn(1.f, fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])));
+        if (!__any_sync(FULL, mn < th)) return false;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            d[i] = (TAIL && i >= lim) ? __int_as_float(0x7f800000) : __fsub_rn(1.f, v[i]);
+    } else {
+        // |b|^2 - 2<a,b> in one rounding (2<a,b> is exact, so the fma rounds
+        // the same value the reference's two operations do); adding |a|^2 and
+        // the clamp at 0 are monotone, so they move to after the min.
+        float e[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            e[i] = (TAIL && i >= lim) ? __int_as_float(0x7f800000) : __fmaf_rn(-2.f, v[i], nrm[i]);
+        float m[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m[i] = fminf(e[2 * i], e[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m[i] = fminf(m[2 * i], m[2 * i + 1]);
+        mn = __fadd_rn(fminf(fminf(m[0], m[1]), fminf(m[2], m[3])), an);
+        mn = mn < 0.f ? 0.f : mn;
+        if (!__any_sync(FULL, mn < th)) return false;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float x = __fadd_rn(e[i], an);
+            d[i] = (TAIL && i >= lim) ? __int_as_float(0x7f800000) : (x < 0.f ? 0.f : x);
+        }
     }
-    float m[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m[i] = fminf(d[2 * i], d[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) m[i] = fminf(m[2 * i], m[2 * i + 1]);
-    const float mn = fminf(fminf(m[0], m[1]), fminf(m[2], m[3]));
-    if (!__any_sync(FULL, mn < th)) return false;
     unsigned mk = 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) mk |= (d[i] < th ? 1u : 0u) << i;

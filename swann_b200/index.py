@@ -237,6 +237,8 @@ class Index:
                     # block is searched as one, so its locality order spans the
                     # whole block.
                     comp = torch.cuda.current_stream(r.dev)
+                    # the shared tables are cleared while the queries cross the link
+                    prep = self._prepare_ahead(r, b - a, cfg, Hc)
                     side = self._copy_stream(r.dev)
                     buf = torch.empty((b - a, host.shape[1]), dtype=host.dtype, device=r.dev)
                     side.wait_stream(comp)   # buf's memory is ready on the search stream
@@ -256,7 +258,7 @@ class Index:
                                                      metric=self._m))
                     if Qd is None:
                         Qd = buf.float().contiguous()
-                    self._search_part(r, Qd, k, cfg, Hc, outs, checks, ent=torch.cat(ents))
+                    self._search_part(r, Qd, k, cfg, Hc, outs, checks, ent=torch.cat(ents), prep=prep)
                 else:
                     src = host if host is not None else queries
                     part = src[a:b] if order is None else src[order[a:b]]
@@ -286,24 +288,33 @@ class Index:
             ids, dist = ids_in, dist_in
         return ids, dist
 
-    def _search_part(self, r, Qd, k, cfg, Hc, outs, checks, ent=None):
+    def _prepare_ahead(self, r, nq, cfg, Hc):
+        """When a block of `nq` queries runs as one launch: clear that launch's
+        shared tables on a side stream, beside the work queued after this call
+        (copies, seed selection), and return the event the launch waits on;
+        None otherwise."""
+        step = max(1, min(nq, TABLE_BUDGET // (8 * Hc)))
+        if nq < PREPARE_AHEAD_MIN or step != nq:
+            return None
+        side = self._side_stream(r.dev, "prepare")
+        side.wait_stream(torch.cuda.current_stream(r.dev))
+        E.prepare_lean(nq, cfg.branches, cfg.budget, r.G.shape[1], r.dev, side, table_slots=Hc)
+        prep = torch.cuda.Event()
+        prep.record(side)
+        return prep
+
+    def _search_part(self, r, Qd, k, cfg, Hc, outs, checks, ent=None, prep=False):
         """Seed selection and the fused search of one device-resident block of
         queries, in table-budget sized launches (and locality order, see
         `locality`); appends (ids, dist) in input order to `outs` and each
         launch's (replica, counters) to `checks`.  `ent`: the seeds' catalogue
-        indices when already selected."""
+        indices when already selected; `prep`: the event of a `_prepare_ahead`
+        already issued for this block (False: issue it here)."""
         nq = Qd.shape[0]
         step = max(1, min(nq, TABLE_BUDGET // (8 * Hc)))
-        prep = None
-        if nq >= PREPARE_AHEAD_MIN and step == nq:
-            # one launch: clear its shared tables on a side stream while the
-            # seeds are selected and sorted
-            comp = torch.cuda.current_stream(r.dev)
-            side = self._side_stream(r.dev, "prepare")
-            side.wait_stream(comp)
-            E.prepare_lean(nq, cfg.branches, cfg.budget, r.G.shape[1], r.dev, side, table_slots=Hc)
-            prep = torch.cuda.Event()
-            prep.record(side)
+        if prep is False:
+            # the tables are cleared while the seeds are selected and sorted
+            prep = self._prepare_ahead(r, nq, cfg, Hc)
         if ent is None:
             ent = S.select_nearest(Qd, r.cat_rows, cfg.branches, metric=self._m)
         seeds = r.catalogue[ent].to(torch.int32)

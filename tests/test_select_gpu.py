@@ -77,3 +77,81 @@ def test_select_matches_on_index_catalogue():
     got = S.select_nearest(Qg, idx._cat, 32, metric=0).cpu()
     want_i, want_v, c = _reference(Qg, idx._cat, 32, 0, 8192)
     _check(got, want_i, want_v, c)
+
+
+def _topk_direct(sc, Ek, metric, vn=None, qn=None, slices=1):
+    """swb_select_topk over the score matrix `sc` [n, P] in `slices` column
+    slices (the later ones resuming the running list)."""
+    from swann_b200 import _lib as N
+    n, P = sc.shape
+    bd = torch.empty((n, Ek), dtype=torch.float32, device=DEV)
+    bi = torch.empty((n, Ek), dtype=torch.int64, device=DEV)
+    bounds = np.linspace(0, P, slices + 1).astype(int)
+    for k, (a, b) in enumerate(zip(bounds[:-1], bounds[1:])):
+        part = sc[:, a:b].contiguous()
+        v = vn[a:b].contiguous() if vn is not None else None
+        rc = N.lib().swb_select_topk(N.ptr(part), n, b - a, part.stride(0), N.ptr(v), N.ptr(qn), int(metric), Ek,
+                                     int(a), N.ptr(bd), N.ptr(bi), int(k > 0), N.stream_of(part))
+        N.check(rc, "swb_select_topk")
+    torch.cuda.synchronize()
+    return bd.cpu(), bi.cpu()
+
+
+def _exact(sc, Ek, metric, vn=None, qn=None):
+    """The Ek smallest (distance, column) keys per row, computed on the CPU in
+    float32 with the same expressions; equal distances go to the lower column."""
+    sc = sc.cpu()
+    if metric == E.METRIC_IP:
+        d = 1.0 - sc
+    else:
+        d = (vn.cpu().view(1, -1) - 2.0 * sc) + qn.cpu().view(-1, 1)
+    cols = torch.arange(sc.shape[1]).expand_as(d)
+    # a stable sort by distance keeps equal distances in column order
+    order = torch.sort(d, dim=1, stable=True).indices
+    k = min(Ek, sc.shape[1])
+    return torch.gather(d, 1, order[:, :k]), torch.gather(cols, 1, order[:, :k])
+
+
+def _layout(kind, n, P, g):
+    """Score matrices built to stress the selection: `lane` puts every row's
+    best scores in the columns one lane of the warp reads (4 of every 128),
+    `trend` makes each row's scores rise (distances fall) along the row, `ties`
+    draws from a handful of values, `random` is plain Gaussian."""
+    if kind == "random":
+        return torch.randn((n, P), generator=g)
+    if kind == "trend":
+        return torch.linspace(-1, 1, P).view(1, -1) + 1e-3 * torch.randn((n, P), generator=g)
+    if kind == "ties":
+        return torch.randint(0, 6, (n, P), generator=g).float() / 8
+    sc = torch.randn((n, P), generator=g) - 4.0
+    cols = torch.arange(P)
+    owner = (cols % 128) // 4                     # the lane that reads each column
+    lane = torch.randint(0, 32, (n, 1), generator=g)
+    return torch.where(owner.view(1, -1) == lane, sc + 8.0, sc)
+
+
+@pytest.mark.parametrize("kind", ["lane", "trend", "ties", "random"])
+@pytest.mark.parametrize("metric", [E.METRIC_IP, E.METRIC_L2])
+@pytest.mark.parametrize("Ek,P,slices", [(32, 4096, 1), (32, 4096, 3), (5, 1000, 1), (64, 2500, 2), (128, 4096, 1),
+                                          (48, 37, 1), (128, 300, 2)])
+def test_select_topk_exact_on_stressed_scores(kind, metric, Ek, P, slices):
+    """swb_select_topk equals the exact (distance, column) order bit for bit on
+    rows built against its filter-and-merge: best entries all in one lane's
+    columns, distances falling along the row (nearly every column survives the
+    filter, so the list is merged once per 32 columns), and heavy ties (the
+    lower column first), over one slice or several resumed ones."""
+    g = torch.Generator(device="cpu").manual_seed(11 + Ek + P + slices)
+    n = 300
+    sc = _layout(kind, n, P, g)
+    vn = qn = None
+    if metric == E.METRIC_L2:
+        vn = torch.rand((P,), generator=g) * 4
+        qn = torch.rand((n,), generator=g) * 4
+        vn, qn = vn.to(DEV), qn.to(DEV)
+    bd, bi = _topk_direct(sc.to(DEV), Ek, metric, vn, qn, slices)
+    want_d, want_i = _exact(sc, Ek, metric, vn, qn)
+    k = want_i.shape[1]
+    assert torch.equal(bi[:, :k], want_i)
+    assert torch.equal(bd[:, :k], want_d)
+    if k < Ek:
+        assert bool((bi[:, k:] == -1).all())
