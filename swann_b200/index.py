@@ -384,8 +384,10 @@ class Index:
                 f"dtype={self.X.dtype}, devices={len(self._replicas)})")
 
 
-# catalogues up to this size get a locality tour (an O(P^2) pass, once)
+# catalogues up to this size get a greedy walk over every entry (an O(P^2) pass,
+# once); larger ones a two-level tour over TOUR_COARSE walked entries
 TOUR_MAX = 16384
+TOUR_COARSE = 4096
 # measured-claims table sizing: slots = TABLE_HEADROOM x the most slots one query
 # claimed so far, a power of two, at least TABLE_MIN (load <= 67% for the
 # busiest query seen, ~15% for a typical one at C3)
@@ -412,21 +414,48 @@ def _claims_key(branches, budget, queue, stop_eps, degree):
 
 
 def _catalogue_tour(cat_rows, metric):
-    """Each catalogue entry's position on a greedy nearest-neighbour tour of the
-    catalogue (int64 [P]), or None when the catalogue is too large: sorting
-    queries by their nearest entry's position keeps queries whose entries are
-    close -- not only equal -- side by side."""
+    """Each catalogue entry's position on a locality tour of the catalogue
+    (int64 [P]), or None for fewer than two entries: sorting queries by their
+    nearest entry's position keeps queries whose entries are close -- not only
+    equal -- side by side.  Up to TOUR_MAX entries the tour is a greedy
+    nearest-neighbour walk over the whole catalogue (an O(P^2) pass, once).
+    Beyond that, TOUR_COARSE entries spread over the catalogue are walked that
+    way, every entry joins its nearest walked entry's cell, and the tour runs
+    cell by cell along the coarse walk (entries of one cell in catalogue
+    order): queries that share a cell, or start in neighbouring cells, run
+    side by side."""
     P = cat_rows.shape[0]
-    if P < 2 or P > TOUR_MAX:
+    if P < 2:
         return None
     V = cat_rows.float()
     with torch.no_grad():
-        if metric == METRICS["ip"]:
-            D = 1.0 - V @ V.T
-        else:
-            vn = (V * V).sum(1)
-            D = vn[:, None] - 2.0 * (V @ V.T) + vn[None, :]
-        D = D.cpu().numpy()
+        if P <= TOUR_MAX:
+            return torch.from_numpy(_greedy_walk(_entry_distances(V, V, metric).cpu().numpy()))
+        pick = torch.linspace(0, P - 1, TOUR_COARSE, device=V.device).round().long()
+        C = V[pick]
+        cpos = torch.from_numpy(_greedy_walk(_entry_distances(C, C, metric).cpu().numpy())).to(V.device)
+        cell = torch.empty(P, dtype=torch.int64, device=V.device)
+        for s in range(0, P, 8192):
+            cell[s:s + 8192] = cpos[_entry_distances(V[s:s + 8192], C, metric).argmin(1)]
+        ids = torch.arange(P, device=V.device)
+        order = torch.argsort(cell * P + ids)
+        pos = torch.empty_like(order)
+        pos[order] = ids
+    return pos.cpu()
+
+
+def _entry_distances(A, B, metric):
+    """[len(A), len(B)] distances in the corpus metric (fp32 matmul: only an
+    ordering heuristic depends on them)."""
+    if metric == METRICS["ip"]:
+        return 1.0 - A @ B.T
+    return (A * A).sum(1)[:, None] - 2.0 * (A @ B.T) + (B * B).sum(1)[None, :]
+
+
+def _greedy_walk(D):
+    """Positions (int64 [P]) along a greedy nearest-neighbour walk from entry 0
+    over the distance matrix D [P, P] (numpy)."""
+    P = D.shape[0]
     pos = np.empty(P, np.int64)
     seen = np.zeros(P, bool)
     cur = 0
@@ -436,7 +465,7 @@ def _catalogue_tour(cat_rows, metric):
         if i + 1 < P:
             row = np.where(seen, np.inf, D[cur])
             cur = int(np.argmin(row))
-    return torch.from_numpy(pos)
+    return pos
 
 
 def _search_device(r: _Replica, Qd, seeds, k, cfg, metric, table_slots, prepared=False):

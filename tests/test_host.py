@@ -156,3 +156,39 @@ def test_bench_corpus_row_blocks_equal_the_whole():
     for a, b in ((0, 1), (70_000, 140_000), (65_535, 65_537), (131_071, 150_000)):
         part = bench.gen_mixture(150_000, 8, 7, 1, torch.device("cpu"), False, True, rows=(a, b))
         assert torch.equal(part, full[a:b]), (a, b)
+
+
+@pytest.mark.parametrize("metric", ["ip", "l2"])
+def test_two_level_tour_orders_cells_along_the_coarse_walk(monkeypatch, metric):
+    """A catalogue above TOUR_MAX gets the two-level tour: a permutation in
+    which every cell (the entries nearest one walked entry) is contiguous, the
+    cells follow the coarse walk, and consecutive entries are near each other."""
+    from swann_b200 import index as I
+    monkeypatch.setattr(I, "TOUR_MAX", 300)
+    monkeypatch.setattr(I, "TOUR_COARSE", 64)
+    g = torch.Generator().manual_seed(3)
+    centres = torch.randn((40, 16), generator=g) * 3
+    V = centres[torch.randint(0, 40, (2000,), generator=g)] + 0.3 * torch.randn((2000, 16), generator=g)
+    if metric == "ip":
+        V = V / V.norm(dim=1, keepdim=True)
+    m = I.METRICS[metric]
+    pos = I._catalogue_tour(V, m)
+    assert torch.equal(torch.sort(pos).values, torch.arange(2000))
+    walk = torch.argsort(pos)                       # entries in tour order
+    C = V[torch.linspace(0, 1999, 64).round().long()]
+    cpos = torch.from_numpy(I._greedy_walk(I._entry_distances(C, C, m).numpy()))
+    cell = cpos[I._entry_distances(V, C, m).argmin(1)]
+    along = cell[walk]
+    assert bool((along[1:] >= along[:-1]).all())    # cells in coarse-walk order, each contiguous
+    D = I._entry_distances(V, V, m)
+    step = D[walk[:-1], walk[1:]].mean()
+    rand = D[torch.randint(0, 2000, (4000,), generator=g), torch.randint(0, 2000, (4000,), generator=g)].mean()
+    assert float(step) < 0.5 * float(rand)
+
+
+def test_small_catalogue_tour_is_the_greedy_walk():
+    from swann_b200 import index as I
+    g = torch.Generator().manual_seed(4)
+    V = torch.randn((200, 8), generator=g)
+    pos = I._catalogue_tour(V, I.METRICS["l2"])
+    assert torch.equal(pos, torch.from_numpy(I._greedy_walk(I._entry_distances(V, V, I.METRICS["l2"]).numpy())))
