@@ -140,7 +140,11 @@ SWB_API int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int
  *   out_ids/out_dist [Q, k] (out)
  *   ids/dist/expanded/lineage/counters: optional outputs of the final branch
  *   states (NULL to skip), shapes as in swb_search_init
- *   status: as in swb_search_advance (never written; NULL is fine) */
+ *   status: as in swb_search_advance (never written; NULL is fine)
+ * A launch of at most 4 x 4 CTAs an SM (a CTA holds 4 branches of one query)
+ * runs the kernel's small-batch form, which holds eight rows a team in flight
+ * instead of two; the results are the same.  The environment variable
+ * SWB_WIDE_CTAS overrides that limit (0: never). */
 SWB_API int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim,
                      const int32_t* G, int D, const float* Qv, const int32_t* seeds,
                      int Q, int J, int V, int k, int L, int B,

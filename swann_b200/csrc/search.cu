@@ -234,17 +234,17 @@ __device__ __forceinline__ uint64_t cache_pack(int v, float d) {
 #define SWB_ROWS 2
 #endif
 
-// Scores the m rows listed in w.w_v into w.w_d, SWB_ROWS * 32/TEAM rows per
-// round: each team reads SWB_ROWS rows from global memory into registers and
-// sums them side by side (common.cuh team_partial_rows); the latency is hidden
-// by the other warps of the SM.  Rows with w.w_slot >= 0 are published to the
-// per-query table `ctab` as soon as they are scored.
-template <int TEAM, typename XT>
+// Scores the m rows listed in w.w_v into w.w_d, R * 32/TEAM rows per round:
+// each team reads R rows from global memory into registers, SEG 16-byte chunks
+// of each at a time, and sums them side by side (common.cuh
+// team_partial_rows; a row's sum does not depend on R or SEG); the latency is
+// hidden by the other warps of the SM.  Rows with w.w_slot >= 0 are published
+// to the per-query table `ctab` as soon as they are scored.
+template <int TEAM, typename XT, int R = SWB_ROWS, int SEG = SWB_LDG_SEG>
 __device__ void score_rows(const Knobs& K, const WarpMem& w, int m, const float* sq, uint64_t* ctab, int lane) {
     constexpr int P = 32 / TEAM;
     const int team = lane / TEAM, tl = lane % TEAM;
     const XT* X = reinterpret_cast<const XT*>(K.X);
-    constexpr int R = SWB_ROWS;
     for (int base = 0; base < m; base += R * P) {
         const int i0 = base + team;
         float acc[R];
@@ -259,13 +259,13 @@ __device__ void score_rows(const Knobs& K, const WarpMem& w, int m, const float*
         if (nrows > 0) {
 #if SWB_ROW_PREFETCH
             // rows longer than one segment: the later segments hit L2
-            if (K.rowbytes > TEAM * SWB_LDG_SEG * 16 && tl < nrows) {
+            if (K.rowbytes > TEAM * SEG * 16 && tl < nrows) {
 #pragma unroll
                 for (int r = 0; r < R; ++r)
                     if (tl == r) prefetch_row_l2(rows[r], (uint32_t)K.rowbytes);
             }
 #endif
-            team_partial_rows<TEAM, XT, R, SWB_LDG_SEG>(sq, rows, nrows, K.dim, K.metric, tl, acc);
+            team_partial_rows<TEAM, XT, R, SEG>(sq, rows, nrows, K.dim, K.metric, tl, acc);
         } else {
 #pragma unroll
             for (int r = 0; r < R; ++r) acc[r] = 0.f;
@@ -417,7 +417,7 @@ __device__ __forceinline__ void swap_queue(WarpMem& w) {
 
 // Seeds -> sorted queue (local_search.cu:318-350).  Duplicate seeds keep their
 // first occurrence (the CPU reference's rule, _refcpu.py:68-74).
-template <int TEAM, typename XT>
+template <int TEAM, typename XT, int R = SWB_ROWS, int SEG = SWB_LDG_SEG>
 __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ctr& ctr) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     if (vis) {
@@ -458,7 +458,7 @@ __device__ void init_branch(const Knobs& K, WarpMem& w, int q, int j, int lane, 
     }
     for (int off = 16; off > 0; off >>= 1) fails += __shfl_xor_sync(FULL, fails, off);
     __syncwarp();
-    score_rows<TEAM, XT>(K, w, m, sq, nullptr, lane);
+    score_rows<TEAM, XT, R, SEG>(K, w, m, sq, nullptr, lane);
     ctr.add(lane, 1, m);
     ctr.add(lane, 2, fails);
     for (int t = lane; t < m; t += 32) {
@@ -564,7 +564,7 @@ __device__ int code_filter(const Knobs& K, const WarpMem& w, int m, const float*
 // codes are given); the fused search never uses it.
 // NT: neighbour slots per lane (the graph degree is at most 32 * NT); 2 for
 // degree <= 64 keeps half the per-neighbour registers of 4.
-template <int TEAM, typename XT, int NT, bool CODES = false>
+template <int TEAM, typename XT, int NT, bool CODES = false, int R = SWB_ROWS, int SEG = SWB_LDG_SEG>
 __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const float* sq, Ctr& ctr, int delta) {
     int* vis = (K.H > 1) ? K.visited + ((size_t)q * K.J + j) * (size_t)K.H : nullptr;
     uint64_t* ctab = (K.Hc > 0) ? K.cache + (size_t)q * (size_t)K.Hc : nullptr;
@@ -709,7 +709,7 @@ __device__ void walk(const Knobs& K, WarpMem& w, int q, int j, int lane, const f
             // Its one trace is the fan-out count (counter 8), kept here too.
             if (worst == FLT_MAX) fanout_extra = skipped;
         }
-        score_rows<TEAM, XT>(K, w, m, sq, ctab, lane);
+        score_rows<TEAM, XT, R, SEG>(K, w, m, sq, ctab, lane);
         for (int b = 0; b < m; b += 32) {
             const int i = b + lane;
             const float d = (i < m) ? w.w_d[i] : FLT_MAX;
@@ -941,8 +941,22 @@ __device__ void merge_sorted_lists(const int32_t* bi, const float* bd, int J, in
 #ifndef SWB_FUSED_MINB
 #define SWB_FUSED_MINB 12
 #endif
-template <int TEAM, typename XT, int NT>
-__global__ void __launch_bounds__(SWB_FUSED_THREADS, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
+// Small batches: when a batch's branches (nearly) all fit on the GPU at once,
+// the time is the longest branch's chain of dependent expansions, not
+// bandwidth, so the wide form scores SWB_WIDE_ROWS rows a team, SWB_WIDE_SEG
+// chunks of each in flight, with the registers that takes (SWB_WIDE_MINB
+// CTAs an SM).  Same arithmetic, same results.
+#ifndef SWB_WIDE_ROWS
+#define SWB_WIDE_ROWS 8
+#endif
+#ifndef SWB_WIDE_SEG
+#define SWB_WIDE_SEG 2
+#endif
+#ifndef SWB_WIDE_MINB
+#define SWB_WIDE_MINB 4
+#endif
+template <int TEAM, typename XT, int NT, int R, int SEG>
+__device__ __forceinline__ void fused_body(const Knobs& K) {
     extern __shared__ __align__(128) char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.y;
@@ -955,8 +969,8 @@ __global__ void __launch_bounds__(SWB_FUSED_THREADS, SWB_FUSED_MINB) fused_kerne
     const Layout lay = warp_layout(K.L, 0, K.cmax);
     WarpMem w = carve(smem + qbytes + (size_t)warp * K.warp_bytes, lay);
     Ctr ctr;
-    init_branch<TEAM, XT>(K, w, q, j, lane, sq, ctr);
-    walk<TEAM, XT, NT>(K, w, q, j, lane, sq, ctr, K.max_exp);
+    init_branch<TEAM, XT, R, SEG>(K, w, q, j, lane, sq, ctr);
+    walk<TEAM, XT, NT, false, R, SEG>(K, w, q, j, lane, sq, ctr, K.max_exp);
     __syncwarp();
     const size_t bid = (size_t)q * K.J + j;
     store_state(K, w, bid, lane, ctr);
@@ -974,6 +988,16 @@ __global__ void __launch_bounds__(SWB_FUSED_THREADS, SWB_FUSED_MINB) fused_kerne
     // the walk is over: w_v .. w_aux (4 * cmax >= J ints, contiguous) hold the heads
     merge_sorted_lists(K.branch_ids + (size_t)q * K.J * K.kk, K.branch_dist + (size_t)q * K.J * K.kk, K.J, K.kk,
                        K.k, w.w_v, K.out_ids + (size_t)q * K.k, K.out_dist + (size_t)q * K.k, lane);
+}
+
+template <int TEAM, typename XT, int NT>
+__global__ void __launch_bounds__(SWB_FUSED_THREADS, SWB_FUSED_MINB) fused_kernel(const __grid_constant__ Knobs K) {
+    fused_body<TEAM, XT, NT, SWB_ROWS, SWB_LDG_SEG>(K);
+}
+
+template <int TEAM, typename XT, int NT>
+__global__ void __launch_bounds__(SWB_FUSED_THREADS, SWB_WIDE_MINB) fused_wide_kernel(const __grid_constant__ Knobs K) {
+    fused_body<TEAM, XT, NT, SWB_WIDE_ROWS, SWB_WIDE_SEG>(K);
 }
 
 __global__ void prepare_kernel(int Q, uint64_t* cache, int64_t cache_words, float* bound, int32_t* qdone) {
@@ -1267,6 +1291,14 @@ extern "C" int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim, 
     K.W = W;
     dim3 grid((unsigned)((J + W - 1) / W), (unsigned)Q);
     const size_t smem = (size_t)query_bytes(dim) + (size_t)W * K.warp_bytes;
+    // the wide form up to four of its waves: measured at C3 (team 16), 2048
+    // CTAs ran 21-23% faster wide (batch 64 x 128 branches, 128 x 64), 8192
+    // CTAs 15% slower (batch 512 x 64); batch 1-16 x 128 branches 25-31% faster
+    const long long ctas = (long long)grid.x * grid.y;
+    const long long wide_max = abi::env_int("SWB_WIDE_CTAS", abi::num_sms() * SWB_WIDE_MINB * 4);
+    if (ctas <= wide_max)
+        return SWB_DISPATCH_NT(fused_wide_kernel, team, slots_for(D), x_dtype, grid, W * 32, smem,
+                               (cudaStream_t)stream, K);
     return SWB_DISPATCH_NT(fused_kernel, team, slots_for(D), x_dtype, grid, W * 32, smem, (cudaStream_t)stream, K);
 }
 

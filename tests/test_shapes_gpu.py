@@ -4,8 +4,8 @@ The headline configurations score 960-wide fp32 rows (L2) and 1536-wide fp16
 rows (inner product), and the north star asks for rows up to 4096 wide.  At
 those widths every lane of a team sums many 16-byte chunks (12 at d = 1536
 fp16 with team 16), the fused kernel scores two rows per team at once and
-keeps an fp16 corpus's query as two planes -- none of which the toy width (64)
-exercises.  Here the fused kernel (the one Index.search launches) is held bit
+keeps an fp16 corpus's query as two planes (eight rows a team in its
+small-batch form) -- none of which the toy width (64) exercises.  Here the fused kernel (the one Index.search launches) is held bit
 for bit against the C oracle and the reference's own compiled kernels at those
 widths and the production knobs, and the production mode's recall on a
 C3-shaped corpus is held to the reference kernel's.
@@ -51,13 +51,17 @@ def queries(nq, d, metric, seed):
     return np.random.default_rng(seed).standard_normal((nq, d), dtype=np.float32)
 
 
+@pytest.mark.parametrize("form", ["wide", "narrow"])
 @pytest.mark.parametrize("d,half,metric,team", SHAPES)
 @pytest.mark.parametrize("L,B,eps", [(12, 64, 0.01), (32, 12, -1.0)])
-def test_fused_walk_bitwise_at_production_widths(d, half, metric, team, L, B, eps):
+def test_fused_walk_bitwise_at_production_widths(d, half, metric, team, L, B, eps, form, monkeypatch):
     """Per-branch queues, distances, flags and counters of the fused kernel
     equal the oracle's single-branch walk (swann/_refcpu.py's semantics) and
     the reference kernels' init_states + advance, bit for bit; the merged
-    answers equal the oracle's."""
+    answers equal the oracle's.  Both forms of the kernel: the wide one small
+    batches get (eight rows a team in flight) and the one large batches get
+    (two), chosen here through SWB_WIDE_CTAS."""
+    monkeypatch.setenv("SWB_WIDE_CTAS", "1000000" if form == "wide" else "0")
     X, G = corpus(d, half, metric)
     nq, J = 6, 4
     Qv = queries(nq, d, metric, 31 + d)
