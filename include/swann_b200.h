@@ -141,10 +141,11 @@ SWB_API int swb_search_prepare(int Q, uint64_t* cache, int Hc, float* bound, int
  *   ids/dist/expanded/lineage/counters: optional outputs of the final branch
  *   states (NULL to skip), shapes as in swb_search_init
  *   status: as in swb_search_advance (never written; NULL is fine)
- * A launch of at most 4 x 4 CTAs an SM (a CTA holds 4 branches of one query)
- * runs the kernel's small-batch form, which holds eight rows a team in flight
- * instead of two; the results are the same.  The environment variable
- * SWB_WIDE_CTAS overrides that limit (0: never). */
+ * Small batches run other forms of the kernel, with the same results: with
+ * Q * J at most 16 an SM, one branch a CTA whose other three warps score its
+ * rows with it; else with at most 16 CTAs an SM (a CTA holds 4 branches of
+ * one query), eight rows a team in flight instead of two.  The environment
+ * variables SWB_HELP_CTAS and SWB_WIDE_CTAS override those limits (0: never). */
 SWB_API int swb_search_fused(const void* X, int x_dtype, int64_t n, int dim,
                      const int32_t* G, int D, const float* Qv, const int32_t* seeds,
                      int Q, int J, int V, int k, int L, int B,

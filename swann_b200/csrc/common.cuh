@@ -109,6 +109,14 @@ __device__ __forceinline__ unsigned lanemask_lt() {
     return m;
 }
 
+// bar.sync on named barrier `id` (1..15; 0 is __syncthreads') for `threads`
+// threads, a multiple of 32, called by whole warps; orders shared-memory
+// accesses like __syncthreads
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+    __syncwarp();
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // -- distances ------------------------------------------------------------
 //
 // The reference fixes the arithmetic (local_search.cu:185-203, _refcpu.py:21-48):

@@ -51,16 +51,18 @@ def queries(nq, d, metric, seed):
     return np.random.default_rng(seed).standard_normal((nq, d), dtype=np.float32)
 
 
-@pytest.mark.parametrize("form", ["wide", "narrow"])
+@pytest.mark.parametrize("form", ["helped", "wide", "narrow"])
 @pytest.mark.parametrize("d,half,metric,team", SHAPES)
 @pytest.mark.parametrize("L,B,eps", [(12, 64, 0.01), (32, 12, -1.0)])
 def test_fused_walk_bitwise_at_production_widths(d, half, metric, team, L, B, eps, form, monkeypatch):
     """Per-branch queues, distances, flags and counters of the fused kernel
     equal the oracle's single-branch walk (swann/_refcpu.py's semantics) and
     the reference kernels' init_states + advance, bit for bit; the merged
-    answers equal the oracle's.  Both forms of the kernel: the wide one small
-    batches get (eight rows a team in flight) and the one large batches get
-    (two), chosen here through SWB_WIDE_CTAS."""
+    answers equal the oracle's.  Every form of the kernel: the helped one the
+    smallest batches get (one branch a CTA, its other warps scoring with it),
+    the wide one small batches get (eight rows a team in flight) and the one
+    large batches get (two), chosen here through SWB_HELP_CTAS / SWB_WIDE_CTAS."""
+    monkeypatch.setenv("SWB_HELP_CTAS", "1000000" if form == "helped" else "0")
     monkeypatch.setenv("SWB_WIDE_CTAS", "1000000" if form == "wide" else "0")
     X, G = corpus(d, half, metric)
     nq, J = 6, 4
