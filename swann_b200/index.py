@@ -265,12 +265,17 @@ class Index:
                     Qd = part.to(r.dev, non_blocking=True).float().contiguous()
                     self._search_part(r, Qd, k, cfg, Hc, outs, checks)
         overflow = 0
+        # The visited tables are elided whenever a query has more than one
+        # branch (the claims table does their job), and then no insert can
+        # fail: the overflow check has nothing to read, so it is not waited
+        # for, and a caller's next batch can be queued behind this one.
+        guard = E._OVERFLOW_GUARD and cfg.branches <= 1
         for r, ctr in checks:
             key = _claims_key(cfg.branches, cfg.budget, cfg.queue, cfg.stop_eps, r.G.shape[1])
             # the most table slots one query claimed (its branches' claims plus
             # their seeds), and the visited-table overflow count
             claims = (ctr[..., 5].to(torch.int64).sum(1) + ctr.shape[1]).max()
-            if E._OVERFLOW_GUARD:
+            if guard:
                 fails, most = torch.stack([ctr[..., 2].to(torch.int64).sum(), claims]).tolist()
                 overflow += fails
                 self._note_claims(key, claims, host_value=most)
