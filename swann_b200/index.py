@@ -225,6 +225,7 @@ class Index:
         # host batches keep contiguous shards, each copied over its own GPU's link.
         order = self.route(queries) if (len(reps) > 1 and host is None) else None
         outs, checks = [], []
+        landed = []   # host batches: an event after each replica's copies
         for r, (a, b) in zip(reps, zip(bounds[:-1], bounds[1:])):
             if b <= a:
                 continue
@@ -250,6 +251,7 @@ class Index:
                             ev = torch.cuda.Event()
                             ev.record(side)
                             ready.append((c0, c1, ev))
+                    landed.append(ready[-1][2])
                     Qd = buf if buf.dtype == torch.float32 else None
                     ents = []
                     for c0, c1, ev in ready:
@@ -263,7 +265,15 @@ class Index:
                     src = host if host is not None else queries
                     part = src[a:b] if order is None else src[order[a:b]]
                     Qd = part.to(r.dev, non_blocking=True).float().contiguous()
+                    if host is not None:
+                        ev = torch.cuda.Event()
+                        ev.record(torch.cuda.current_stream(r.dev))
+                        landed.append(ev)
                     self._search_part(r, Qd, k, cfg, Hc, outs, checks)
+        # The caller may reuse its host buffer once this returns: wait for the
+        # copies out of it (not for the search).
+        for ev in landed:
+            ev.synchronize()
         overflow = 0
         # The visited tables are elided whenever a query has more than one
         # branch (the claims table does their job), and then no insert can

@@ -199,3 +199,22 @@ def test_routed_replicas_answer_in_input_order(ip_index):
     assert np.allclose(dist2, ex, atol=2e-6)
     truth = exact(X, Qb, 10, "ip")
     assert abs(recall(ids2, truth, 10) - recall(ids1.cpu().numpy(), truth, 10)) <= 0.01
+
+
+@pytest.mark.parametrize("nq", [300, 9000])
+def test_host_buffer_is_free_once_search_tensors_returns(ip_index, nq):
+    """search_tensors does not wait for the search, but it does wait for the
+    copies out of a host batch: overwriting the (pinned) host queries right
+    after the call leaves the answers those queries should get (both the
+    one-copy path and the chunked one, above 8192 queries)."""
+    X, _, index = ip_index
+    rng = np.random.default_rng(5)
+    Q = rng.standard_normal((nq, X.shape[1]), dtype=np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    truth = exact(X, Q, 10, "ip")
+    host = torch.from_numpy(Q.copy()).pin_memory()
+    ids, _ = index.search_tensors(host, k=10)
+    host.zero_()
+    got = recall(ids.cpu().numpy(), truth, 10)
+    clean = recall(index.search(Q, k=10)[0], truth, 10)
+    assert got > 0.9 and abs(got - clean) < 0.01
